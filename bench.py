@@ -1,0 +1,415 @@
+#!/usr/bin/env python
+"""Benchmark of tread's chunk-reuse hot path on B200 (one process per GPU).
+
+Workload (the kernel microbench): a pool of 64 cached blocks, each K and
+V of [28 layers, 1, 4 kv heads, 512 tokens, 128] bf16 ~ N(0,1). One step gathers 16 random
+blocks (seeded ids, per-block shift delta uniform in [-16384, 16384]) into a contiguous
+8192-token assembled cache: RoPE re-rotation of K, copy of V, append (tread/engine.py:108-120,
+tread/blend.py:22-39). Algorithmic bytes per step = read K+V + write K+V = 939.5 MB.
+
+  value : GB/s of algorithmic bytes, inputs resident in HBM (the store's GPU tier), whole job
+          (all ranks) / max-over-ranks device time of exactly --steps steps.
+  e2e   : same metric through the C ABI with HOST buffers: each step fetches its 16 blocks
+          from pinned host memory (the store's CPU tier), rotates/appends, and copies the
+          assembled cache back to pinned host memory, all inside the timed region.
+  --impl reference : the reference path's CPU restatement (oracle, all host threads) on the
+          same workload; rank 0 only.
+
+Multi-GPU: every rank assembles its own requests from its own pool (weak scaling, no
+collective on the data path).
+"""
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+import numpy as np
+import torch
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+METRIC = "p50 TTFT @8k reordered RAG, 7B 20% recompute; KV rotate/gather HBM GB/s"
+L, HKV, NTOK, D = 28, 4, 512, 128
+THETA = 1e6
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=200)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="tread_b200", choices=["tread_b200", "reference"])
+    ap.add_argument("--pool", type=int, default=64)
+    ap.add_argument("--blocks", type=int, default=16)
+    ap.add_argument("--e2e-steps", type=int, default=5)
+    ap.add_argument("--seed", type=int, default=0)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--cpu-seconds", type=float, default=10.0, help="CPU baseline sample budget")
+    return ap.parse_args()
+
+
+def algorithmic_bytes(nblk):
+    per_tensor = L * HKV * nblk * NTOK * D * 2  # bf16
+    return 4 * per_tensor  # read K, read V, write K, write V
+
+
+def plan_steps(nsteps, pool, nblk, seed):
+    g = np.random.default_rng(seed)
+    ids = g.integers(0, pool, size=(nsteps, nblk))
+    deltas = g.integers(-16384, 16385, size=(nsteps, nblk))
+    return ids, deltas
+
+
+def inv_freq_list():
+    return (1.0 / (THETA ** (torch.arange(0, D, 2, dtype=torch.int64).to(torch.float) / D))).tolist()
+
+
+# ---------------------------------------------------------------------------------------------
+# clocks
+
+class ClockSampler:
+    """Samples nvidia-smi clocks/throttle reasons every 200 ms for one GPU."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, device):
+        self.samples = []
+        self.proc = None
+        try:
+            uuid = str(torch.cuda.get_device_properties(device).uuid)
+            self.sel = uuid if uuid.startswith("GPU-") else "GPU-" + uuid
+        except Exception:
+            self.sel = None
+
+    def start(self):
+        cmd = ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits", "-lms", "200"]
+        if self.sel:
+            cmd[1:1] = ["-i", self.sel]
+        try:
+            self.proc = subprocess.Popen(cmd, stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            self.proc = None
+            return
+        self.thread = threading.Thread(target=self._read, daemon=True)
+        self.thread.start()
+
+    def _read(self):
+        for line in self.proc.stdout:
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) >= 9:
+                self.samples.append((time.perf_counter(), parts))
+
+    def stop(self, t0=None, t1=None):
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"], "samples": 0}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        self.thread.join(timeout=2)
+        sel = [p for t, p in self.samples if (t0 is None or t >= t0) and (t1 is None or t <= t1)]
+        if not sel:
+            sel = [p for _, p in self.samples]
+        sm, mx, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for p in sel:
+            try:
+                sm.append(float(p[1]))
+                mx.append(float(p[2]))
+            except ValueError:
+                pass
+            for nm, val in zip(names, p[5:9]):
+                if val.lower() == "active":
+                    reasons.add(nm)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
+                "reasons": sorted(reasons), "samples": len(sel)}
+
+
+# ---------------------------------------------------------------------------------------------
+# distributed plumbing
+
+def dist_setup():
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+                                device_id=torch.device("cuda", local))
+    else:
+        torch.cuda.set_device(0)
+    return world, rank, torch.device("cuda", local if world > 1 else 0)
+
+
+def barrier(world):
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.barrier()
+
+
+def max_over_ranks(x, world, device):
+    if world == 1:
+        return x
+    import torch.distributed as dist
+
+    t = torch.tensor([x], dtype=torch.float64, device=device)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+# ---------------------------------------------------------------------------------------------
+# CPU baseline / reference arm: the oracle restatement of rotate_keys + torch.cat
+
+def cpu_assembly_rate(nsteps_min, seconds, seed, nblk, host_pool=16):
+    from oracle import oracle as orc
+
+    g = np.random.default_rng(seed + 7)
+    shape = (L, 1, HKV, NTOK, D)
+    pool = [(orc.f32_to_bf16(g.standard_normal(shape, dtype=np.float32)),
+             orc.f32_to_bf16(g.standard_normal(shape, dtype=np.float32))) for _ in range(host_pool)]
+    ids, deltas = plan_steps(10_000, host_pool, nblk, seed + 11)
+    inv = np.array(inv_freq_list(), np.float32)
+    T = nblk * NTOK
+    out = (np.empty((L, 1, HKV, T, D), np.uint16), np.empty((L, 1, HKV, T, D), np.uint16))
+    threads = orc.max_threads()
+    times = []
+    t_start = time.perf_counter()
+    s = 0
+    while s < nsteps_min or (time.perf_counter() - t_start < seconds and s < 10_000):
+        segs = [(pool[i][0], pool[i][1], int(d), j * NTOK) for j, (i, d) in enumerate(zip(ids[s], deltas[s]))]
+        t0 = time.perf_counter()
+        orc.rope_gather_append(segs, T, inv, nthreads=threads, out=out)
+        times.append(time.perf_counter() - t0)
+        s += 1
+    med = statistics.median(times[1:] if len(times) > 1 else times)
+    return {"gbs": algorithmic_bytes(nblk) / med / 1e9, "ms": med * 1e3, "steps": len(times), "cores": threads,
+            "host_pool": host_pool}
+
+
+def run_reference(args):
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return 0
+    r = cpu_assembly_rate(args.warmup + args.steps, 0.0, args.seed, args.blocks)
+    line = {
+        "impl": "reference", "metric": METRIC, "value": round(r["gbs"], 3), "unit": "GB/s", "n_gpus": args.gpus,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(r["ms"], 3), "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+        "config": workload_config(args),
+        "cpu_baseline": {"value": round(r["gbs"], 3), "unit": "GB/s", "cores": r["cores"], "kind": "port",
+                         "sample": f"median of {r['steps']} full steps ({args.blocks} blocks of "
+                                   f"[{L},1,{HKV},{NTOK},{D}] bf16 from a {r['host_pool']}-block host pool)"},
+        "e2e": {"value": round(r["gbs"], 3), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+def workload_config(args):
+    return {"workload": "configs[1] rotate+gather+append microbench", "pool_blocks": args.pool,
+            "blocks_per_step": args.blocks, "block_shape": [L, 1, HKV, NTOK, D], "assembled_tokens":
+            args.blocks * NTOK, "delta_range": [-16384, 16384], "rope_theta": THETA,
+            "l2": "inputs larger than L2 (939.5 MB touched per step, random blocks from a 1.88 GB pool)",
+            "parallelism": f"dp{args.gpus} (independent replicas)"}
+
+
+# ---------------------------------------------------------------------------------------------
+# GPU arm
+
+def run_gpu(args):
+    from tread_b200 import kernels
+
+    world, rank, dev = dist_setup()
+    torch.manual_seed(args.seed + rank)
+    gen = torch.Generator(device=dev).manual_seed(args.seed + 1000 * rank)
+    shape = (L, 1, HKV, NTOK, D)
+    pool_k = [torch.randn(shape, generator=gen, device=dev, dtype=torch.float32).to(torch.bfloat16)
+              for _ in range(args.pool)]
+    pool_v = [torch.randn(shape, generator=gen, device=dev, dtype=torch.float32).to(torch.bfloat16)
+              for _ in range(args.pool)]
+    T = args.blocks * NTOK
+    out_k = torch.empty((L, 1, HKV, T, D), device=dev, dtype=torch.bfloat16)
+    out_v = torch.empty_like(out_k)
+    inv = inv_freq_list()
+    total = args.warmup + args.steps
+    ids, deltas = plan_steps(max(total, 64), args.pool, args.blocks, args.seed + 17 * rank)
+    plans = [kernels.RopeAppendPlan([(pool_k[i], pool_v[i], int(d), j * NTOK)
+                                     for j, (i, d) in enumerate(zip(ids[s], deltas[s]))], out_k, out_v, inv)
+             for s in range(max(total, 64))]
+    stream = torch.cuda.current_stream(dev)
+    nbytes = algorithmic_bytes(args.blocks)
+
+    clocks = ClockSampler(dev) if rank == 0 else None
+    if clocks:
+        clocks.start()
+    # settle: ~1 s of untimed work so the clock record covers a loaded GPU even for small --steps
+    t_settle = time.perf_counter()
+    s = 0
+    while time.perf_counter() - t_settle < 1.0:
+        plans[s % len(plans)].launch(stream)
+        s += 1
+        if s % 64 == 0:
+            torch.cuda.synchronize(dev)
+    torch.cuda.synchronize(dev)
+    for s in range(args.warmup):
+        plans[s].launch(stream)
+    torch.cuda.synchronize(dev)
+
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
+    barrier(world)
+    torch.cuda.synchronize(dev)
+    t_wall0 = time.perf_counter()
+    start = torch.cuda.Event(enable_timing=True)
+    end = torch.cuda.Event(enable_timing=True)
+    start.record(stream)
+    for s in range(args.steps):
+        ev[s][0].record(stream)
+        plans[(args.warmup + s) % len(plans)].launch(stream)
+        ev[s][1].record(stream)
+    end.record(stream)
+    torch.cuda.synchronize(dev)
+    t_wall1 = time.perf_counter()
+    barrier(world)
+    step_ms = start.elapsed_time(end) / args.steps
+    kern_ms = statistics.fmean(a.elapsed_time(b) for a, b in ev)
+    step_ms_max = max_over_ranks(step_ms, world, dev)
+    kern_ms_max = max_over_ranks(kern_ms, world, dev)
+    clk = clocks.stop(t_wall0 - 1.5, t_wall1 + 0.2) if clocks else None
+
+    e2e = run_e2e(args, dev, pool_k, pool_v, ids, deltas, inv, world, rank)
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        r = cpu_assembly_rate(3, args.cpu_seconds, args.seed, args.blocks)
+        cpu = {"value": round(r["gbs"], 3), "unit": "GB/s", "cores": r["cores"], "kind": "port",
+               "sample": f"median of {r['steps']} full steps (~{args.cpu_seconds:.0f} s) of the same workload, "
+                         f"{args.blocks} blocks from a {r['host_pool']}-block host pool, oracle C restatement"}
+    peaks = load_peaks()
+    achieved = nbytes / (kern_ms_max * 1e-3) / 1e9
+    value = world * nbytes / (step_ms_max * 1e-3) / 1e9
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": round(value, 2), "unit": "GB/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": round(step_ms_max, 5), "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+            "config": workload_config(args),
+            "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peaks["hbm_gbs"],
+                         "unit": "GB/s", "frac": round(achieved / peaks["hbm_gbs"], 4),
+                         "peak_source": peaks["source"], "kernel": "rope_gather_append_kernel<bf16>",
+                         "bytes_per_launch": nbytes, "traffic": TRAFFIC_PER_LAUNCH},
+            "cpu_baseline": cpu,
+            "e2e": e2e,
+            "gpu_launches": args.steps,
+            "clocks": clk,
+        }
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.destroy_process_group()
+    return 0
+
+
+# dram__bytes_read.sum + dram__bytes_write.sum of one launch from an ncu capture of this kernel
+# (profiles/rope_gather_append_cfg2.md); None until captured.
+TRAFFIC_PER_LAUNCH = None
+
+
+def load_peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        with open(p) as f:
+            j = json.load(f)
+        return {"hbm_gbs": float(j["hbm_gbs"]), "source": "measured (MEASURED_PEAKS.json hbm_gbs)"}
+    except Exception:
+        return {"hbm_gbs": 6650.0, "source": "fallback 6.65 TB/s"}
+
+
+def run_e2e(args, dev, pool_k, pool_v, ids, deltas, inv, world, rank):
+    """Host buffers in and out: per step, fetch the 16 blocks from pinned host memory, rotate and
+    append each as soon as it lands, and copy each block's slice of the assembled cache back to
+    pinned host memory; three streams pipeline H2D, kernel and D2H per block."""
+    from tread_b200 import kernels
+
+    nblk = args.blocks
+    nhost = min(args.pool, 32)
+    host_k = [pool_k[i].cpu().pin_memory() for i in range(nhost)]
+    host_v = [pool_v[i].cpu().pin_memory() for i in range(nhost)]
+    T = nblk * NTOK
+    out_k = torch.empty((L, 1, HKV, T, D), device=dev, dtype=torch.bfloat16)
+    out_v = torch.empty_like(out_k)
+    hout_k = torch.empty(out_k.shape, dtype=torch.bfloat16).pin_memory()
+    hout_v = torch.empty(out_v.shape, dtype=torch.bfloat16).pin_memory()
+    stage_k = [torch.empty((L, 1, HKV, NTOK, D), device=dev, dtype=torch.bfloat16) for _ in range(nblk)]
+    stage_v = [torch.empty_like(stage_k[0]) for _ in range(nblk)]
+    s_in, s_cmp, s_out = torch.cuda.Stream(dev), torch.cuda.Stream(dev), torch.cuda.Stream(dev)
+    ev_in = [torch.cuda.Event() for _ in range(nblk)]
+    ev_cmp = [torch.cuda.Event() for _ in range(nblk)]
+    ev_out = [torch.cuda.Event() for _ in range(nblk)]
+    nsteps = 2 + args.e2e_steps
+    plans = [[kernels.RopeAppendPlan([(stage_k[j], stage_v[j], int(deltas[s % len(deltas)][j]), j * NTOK)],
+                                     out_k, out_v, inv) for j in range(nblk)] for s in range(nsteps)]
+    launches = 0
+
+    def step(s):
+        nonlocal launches
+        for j in range(nblk):
+            i = int(ids[s % len(ids)][j]) % nhost
+            s_in.wait_event(ev_cmp[j])  # previous step's kernel finished reading stage j
+            kernels.kv_fetch(stage_k[j], host_k[i], s_in)
+            kernels.kv_fetch(stage_v[j], host_v[i], s_in)
+            ev_in[j].record(s_in)
+            s_cmp.wait_event(ev_in[j])
+            s_cmp.wait_event(ev_out[j])  # previous step's D2H of these rows finished
+            plans[s][j].launch(s_cmp)
+            launches += 1
+            ev_cmp[j].record(s_cmp)
+            s_out.wait_event(ev_cmp[j])
+            kernels.kv_spill_rows(hout_k, out_k, j * NTOK, NTOK, s_out)
+            kernels.kv_spill_rows(hout_v, out_v, j * NTOK, NTOK, s_out)
+            ev_out[j].record(s_out)
+
+    for s in range(2):
+        step(s)
+    torch.cuda.synchronize(dev)
+    barrier(world)
+    launches = 0
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    start.record(s_in)
+    for s in range(args.e2e_steps):
+        step(2 + s)
+    s_out.wait_stream(s_in)
+    s_out.wait_stream(s_cmp)
+    end.record(s_out)
+    torch.cuda.synchronize(dev)
+    ms = start.elapsed_time(end) / args.e2e_steps
+    ms = max_over_ranks(ms, world, dev)
+    blk_bytes = pool_k[0].nbytes + pool_v[0].nbytes
+    return {"value": round(world * algorithmic_bytes(nblk) / (ms * 1e-3) / 1e9, 2), "unit": "GB/s",
+            "ms_per_step": round(ms, 3), "h2d_bytes_per_step": nblk * blk_bytes,
+            "d2h_bytes_per_step": out_k.nbytes + out_v.nbytes, "kernel_launches_per_step": nblk,
+            "path": "pinned host blocks -> tread_kv_fetch -> tread_rope_gather_append -> tread_kv_spill_rows"}
+
+
+def main():
+    args = parse()
+    if args.impl == "reference":
+        return run_reference(args)
+    return run_gpu(args)
+
+
+if __name__ == "__main__":
+    sys.exit(main())

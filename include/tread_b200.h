@@ -1,0 +1,99 @@
+/*
+ * tread_b200 C ABI: B200 (sm_100a) kernels for tread's chunk-reuse hot path.
+ *
+ * The reference (sykeriin/tread) is pure Python/PyTorch and has no FFI; each entry point
+ * below replaces the library-call sequence at the cited reference location, and the
+ * Python host layer (package `tread_b200`) keeps tread's own function signatures on top.
+ *
+ * Conventions for every entry point:
+ *   - returns TREAD_OK (0) or a nonzero status; tread_last_error() then describes it;
+ *   - tensor pointers are DEVICE pointers owned by the caller (PyTorch); arrays documented
+ *     as "host" are read during the call only;
+ *   - all work is stream-ordered on `stream` (a cudaStream_t); no call synchronises the
+ *     host, and none allocates device memory unless its comment says so;
+ *   - no C++ exception crosses the boundary.
+ */
+#ifndef TREAD_B200_H
+#define TREAD_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef struct CUstream_st* tread_stream_t; /* identical to cudaStream_t */
+
+enum {
+  TREAD_OK = 0,
+  TREAD_ERR_INVALID = 1, /* bad argument: nothing was launched */
+  TREAD_ERR_CUDA = 2,    /* CUDA runtime error at launch */
+  TREAD_ERR_TIMEOUT = 3  /* a bounded device-side wait gave up */
+};
+
+/* element type codes for the `dtype` arguments */
+enum { TREAD_F32 = 0, TREAD_F16 = 1, TREAD_BF16 = 2 };
+
+/* Text of the last error raised on the calling host thread ("" if none). */
+const char* tread_last_error(void);
+
+/* ABI revision of this library; bumped on any signature change. */
+int tread_abi_version(void);
+
+/*
+ * Fused gather + RoPE re-rotation + append of cached KV blocks into one assembled cache.
+ *
+ * Replaces, per request, the loop at tread/engine.py:108-120:
+ *   Ks.append(rotate_keys(model, b.K, offset - b.base)); Vs.append(b.V)   (engine.py:112-115)
+ *   K = torch.cat(Ks, dim=-2); V = torch.cat(Vs, dim=-2)                  (engine.py:119-120)
+ * with rotate_keys (tread/blend.py:22-39) computed in fp32:
+ *   angle_i = float(delta) * inv_freq[i]       (fp32 product, as HF rotary_emb)
+ *   c_i = cos(angle_i) * s / s,  s_i = sin(angle_i) * s / s   (s = attention_scaling)
+ *   out[i]       = x[i] * c_i - x[i + D/2] * s_i
+ *   out[i + D/2] = x[i + D/2] * c_i + x[i] * s_i          (rotate_half pairing)
+ * rounded once to the storage type. delta == 0 copies K unchanged (blend.py:32-33).
+ *
+ * Segment j (0 <= j < nseg) is one cached block, K and V each laid out contiguous as
+ * [L, Hkv, n_tok[j], D] (tread/store.py:1-5 layout, batch dim of 1 dropped). Its tokens
+ * land at token rows dst_tok0[j] .. dst_tok0[j] + n_tok[j] - 1 of out_k / out_v, which
+ * are [L, Hkv, T_out, D] contiguous. Segments must not overlap in the output.
+ *
+ *   k_src, v_src : host arrays [nseg] of device pointers (16-byte aligned)
+ *   n_tok        : host [nseg], each >= 0
+ *   delta        : host [nseg] position shift (new offset - base), |delta| < 2^24
+ *   dst_tok0     : host [nseg]
+ *   inv_freq     : host [D/2] fp32 RoPE inverse frequencies (model.rotary_emb.inv_freq)
+ *   attn_scaling : RoPE attention scaling folded into HF cos/sin (1.0 for default RoPE)
+ *   dtype        : TREAD_BF16, TREAD_F16 or TREAD_F32; D * elsize a multiple of 32 bytes
+ */
+int tread_rope_gather_append(const void* const* k_src, const void* const* v_src,
+                             const int32_t* n_tok, const int64_t* delta,
+                             const int64_t* dst_tok0, int nseg, void* out_k, void* out_v,
+                             int L, int Hkv, int D, int64_t T_out, const float* inv_freq,
+                             float attn_scaling, int dtype, tread_stream_t stream);
+
+/*
+ * Block-store tier transfers (pinned host <-> HBM), stream-ordered DMA copies.
+ *
+ * tread_kv_spill replaces the GPU->CPU-tier move of tread/store.py:111
+ * (`b.K.to("cpu").pin_memory()`: a synchronous pageable copy plus a second pinned copy) and
+ * tread_kv_fetch the CPU-tier hit of tread/store.py:75-76 (`b.K.to(b.device,
+ * non_blocking=True)`). Issue them on a transfer stream and order consumers with events so
+ * the copies overlap rotation kernels on the compute stream.
+ * Host buffers must be page-locked (cudaHostAlloc / torch pin_memory); TREAD_ERR_INVALID
+ * otherwise. The *_rows variants copy `nrows` rows of `row_bytes` at the given pitches
+ * (one block's token slice of an assembled [L, Hkv, T, D] cache is L*Hkv such rows).
+ */
+int tread_kv_fetch(void* dst_device, const void* src_host, size_t bytes, tread_stream_t stream);
+int tread_kv_spill(void* dst_host, const void* src_device, size_t bytes, tread_stream_t stream);
+int tread_kv_fetch_rows(void* dst_device, size_t dst_pitch, const void* src_host, size_t src_pitch,
+                        size_t row_bytes, size_t nrows, tread_stream_t stream);
+int tread_kv_spill_rows(void* dst_host, size_t dst_pitch, const void* src_device, size_t src_pitch,
+                        size_t row_bytes, size_t nrows, tread_stream_t stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* TREAD_B200_H */

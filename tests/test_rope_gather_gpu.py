@@ -1,0 +1,154 @@
+"""Parity of the fused gather + RoPE re-rotation + append kernel (tread_rope_gather_append)
+against the reference's fp32 rotation (golden) and the CPU oracle.
+
+Bar (north star): rotated K within 1 bf16 ulp of the reference's fp32 rotation; V and
+zero-shift K bit-exact copies; rows outside the segments untouched.
+"""
+import numpy as np
+import pytest
+import torch
+
+from conftest import golden
+from oracle import oracle as orc
+from tread_b200 import kernels
+
+pytestmark = pytest.mark.gpu
+
+
+def bits_to_torch_bf16(bits, device):
+    return torch.from_numpy(np.ascontiguousarray(bits).view(np.int16)).view(torch.bfloat16).to(device)
+
+
+def torch_bf16_bits(t):
+    return t.detach().cpu().view(torch.int16).numpy().view(np.uint16)
+
+
+def within_one_ulp(got_f32, ref_f32):
+    return np.abs(got_f32 - ref_f32) <= orc.bf16_ulp(ref_f32)
+
+
+@pytest.mark.parametrize("D", [64, 128])
+def test_rotation_within_one_bf16_ulp_of_reference_fp32(cuda, D):
+    g = golden("rope.npz")
+    kb = g[f"d{D}_k_bf16"]
+    inv = g[f"d{D}_inv_freq"]
+    n = kb.shape[-2]
+    K = bits_to_torch_bf16(kb, cuda)
+    for d in g["deltas"]:
+        out_k = torch.empty_like(K)
+        out_v = torch.empty_like(K)
+        kernels.rope_gather_append([(K, K, int(d), 0)], out_k, out_v, inv)
+        torch.cuda.synchronize()
+        got = orc.bf16_to_f32(torch_bf16_bits(out_k))
+        ref = g[f"d{D}_rot_{d}"]
+        assert within_one_ulp(got, ref).all(), f"delta={d}: max |diff| {np.abs(got - ref).max()}"
+        assert torch.equal(out_v, K)
+        if d == 0:
+            assert torch.equal(out_k, K)
+    # fp32 storage: same inputs, fp32 output, compared to the reference's fp32 result
+    Kf = K.float()
+    for d in g["deltas"]:
+        out_k = torch.empty_like(Kf)
+        out_v = torch.empty_like(Kf)
+        kernels.rope_gather_append([(Kf, Kf, int(d), 0)], out_k, out_v, inv)
+        ref = g[f"d{D}_rot_{d}"]
+        np.testing.assert_allclose(out_k.cpu().numpy(), ref, rtol=0, atol=3e-6 * (np.abs(ref).max() + 1))
+
+
+def _random_segments(rng, lead, D, lens, dtype, device, max_delta=16384):
+    segs_t, segs_np = [], []
+    off = int(rng.integers(0, 5))
+    for n in lens:
+        K = torch.from_numpy(rng.standard_normal(lead + (n, D)).astype(np.float32)).to(dtype)
+        V = torch.from_numpy(rng.standard_normal(lead + (n, D)).astype(np.float32)).to(dtype)
+        delta = int(rng.integers(-max_delta, max_delta + 1))
+        if dtype == torch.bfloat16:
+            kn, vn = torch_bf16_bits(K), torch_bf16_bits(V)
+        else:
+            kn, vn = K.numpy(), V.numpy()
+        segs_t.append((K.to(device), V.to(device), delta, off))
+        segs_np.append((kn, vn, delta, off))
+        off += n
+    return segs_t, segs_np, off
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16, torch.float32])
+@pytest.mark.parametrize("D", [64, 128])
+def test_ragged_assembly_matches_oracle(cuda, dtype, D):
+    rng = np.random.default_rng(D + 3)
+    lead = (3, 1, 2)  # [L, 1, Hkv]
+    lens = [1, 63, 64, 65, 0, 250, 129, 7]
+    segs_t, segs_np, total = _random_segments(rng, lead, D, lens, dtype, cuda)
+    segs_t[0] = (segs_t[0][0], segs_t[0][1], 0, segs_t[0][3])  # a zero-shift (prefix) segment
+    segs_np[0] = (segs_np[0][0], segs_np[0][1], 0, segs_np[0][3])
+    T_out = total + 9
+    inv = orc.inv_freq(D, 1e6)
+    sentinel = 3.0
+    out_k = torch.full(lead + (T_out, D), sentinel, dtype=dtype, device=cuda)
+    out_v = torch.full(lead + (T_out, D), sentinel, dtype=dtype, device=cuda)
+    kernels.rope_gather_append(segs_t, out_k, out_v, inv)
+    ref_k, ref_v = orc.rope_gather_append(segs_np, T_out, inv, out_dtype=orc.F32)
+    gk = out_k.float().cpu().numpy()
+    gv = out_v.float().cpu().numpy()
+    covered = np.zeros(T_out, bool)
+    for (_, _, _, d0), n in zip(segs_np, lens):
+        covered[d0:d0 + n] = True
+    assert (gk[..., ~covered, :] == sentinel).all() and (gv[..., ~covered, :] == sentinel).all()
+    ck, rk = gk[..., covered, :], ref_k[..., covered, :]
+    np.testing.assert_array_equal(gv[..., covered, :], ref_v[..., covered, :])
+    if dtype == torch.bfloat16:
+        assert within_one_ulp(ck, rk).all()
+    elif dtype == torch.float16:
+        ulp = np.spacing(np.abs(rk).astype(np.float16)).astype(np.float32)
+        assert (np.abs(ck - rk) <= ulp).all()
+    else:
+        np.testing.assert_allclose(ck, rk, rtol=0, atol=2e-6 * (np.abs(rk).max() + 1))
+    # zero-shift segment is a bit-exact copy
+    n0, d00 = lens[0], segs_np[0][3]
+    assert torch.equal(out_k[..., d00:d00 + n0, :], segs_t[0][0])
+
+
+def test_cfg2_full_size_properties(cuda):
+    """BASELINE configs[1] shapes (pool 64 x [28,1,4,512,128] bf16, 16 blocks -> 8192 tokens):
+    size-independent checks at full size plus an oracle spot check on sampled blocks."""
+    torch.manual_seed(0)
+    L, H, n, D, nblk = 28, 4, 512, 128, 16
+    pool_k = [torch.randn(L, 1, H, n, D, device=cuda, dtype=torch.bfloat16) for _ in range(8)]
+    pool_v = [torch.randn(L, 1, H, n, D, device=cuda, dtype=torch.bfloat16) for _ in range(8)]
+    g = torch.Generator().manual_seed(1)
+    ids = torch.randint(0, 8, (nblk,), generator=g).tolist()
+    deltas = torch.randint(-16384, 16385, (nblk,), generator=g).tolist()
+    T = nblk * n
+    out_k = torch.empty(L, 1, H, T, D, device=cuda, dtype=torch.bfloat16)
+    out_v = torch.empty_like(out_k)
+    inv = orc.inv_freq(D, 1e6)
+    segs = [(pool_k[i], pool_v[i], d, j * n) for j, (i, d) in enumerate(zip(ids, deltas))]
+    kernels.rope_gather_append(segs, out_k, out_v, inv)
+    # V is gathered bit-exactly; rotation preserves each pair's norm (to bf16 rounding)
+    for j, i in enumerate(ids):
+        assert torch.equal(out_v[..., j * n:(j + 1) * n, :], pool_v[i])
+    for j, i in enumerate(ids):
+        src = pool_k[i].float()
+        dst = out_k[..., j * n:(j + 1) * n, :].float()
+        ns = src[..., :D // 2] ** 2 + src[..., D // 2:] ** 2
+        nd = dst[..., :D // 2] ** 2 + dst[..., D // 2:] ** 2
+        assert torch.allclose(nd, ns, rtol=2e-2, atol=1e-3)
+    # rotating back by -delta recovers the source within 2 bf16 ulp
+    back_k = torch.empty_like(out_k)
+    back_v = torch.empty_like(out_v)
+    kernels.rope_gather_append([(out_k[..., j * n:(j + 1) * n, :].contiguous(), out_v[..., j * n:(j + 1) * n, :]
+                                 .contiguous(), -d, j * n) for j, d in enumerate(deltas)], back_k, back_v, inv)
+    for j, i in enumerate(ids):
+        a = back_k[..., j * n:(j + 1) * n, :].float()
+        b = pool_k[i].float()
+        # each rounding step errs by half an ulp of the rotated pair's magnitude, not of the element
+        pair = (b[..., :D // 2] ** 2 + b[..., D // 2:] ** 2).sqrt().repeat(1, 1, 1, 1, 2)
+        ulp = torch.from_numpy(orc.bf16_ulp(pair.cpu().numpy())).to(cuda)
+        assert ((a - b).abs() <= 2 * ulp + 1e-6).all()
+    # oracle spot check on two whole blocks
+    for j in (0, nblk - 1):
+        i = ids[j]
+        kn = torch_bf16_bits(pool_k[i])
+        ref_k, _ = orc.rope_gather_append([(kn, kn, deltas[j], 0)], n, inv, out_dtype=orc.F32)
+        got = orc.bf16_to_f32(torch_bf16_bits(out_k[..., j * n:(j + 1) * n, :].contiguous()))
+        assert within_one_ulp(got, ref_k).all()

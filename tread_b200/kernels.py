@@ -1,0 +1,132 @@
+"""Torch-facing wrappers of the C-ABI kernels (device pointers in, stream-ordered, no host sync).
+
+Each wrapper validates shapes/dtypes/devices on the host and calls the library; there is no
+PyTorch fallback path.
+"""
+import torch
+
+from tread_b200 import _capi as C
+
+
+def _flat_kv(t, name):
+    """A block tensor [L, 1, Hkv, n, D] (tread/store.py layout) or [L, Hkv, n, D] as (LH, n, D)."""
+    C.require_cuda(t, name)
+    if not t.is_contiguous():
+        raise ValueError(f"{name} must be contiguous")
+    return t.shape[-2], t.shape[-1]
+
+
+class RopeAppendPlan:
+    """Validated, pre-marshalled arguments of one tread_rope_gather_append call.
+
+    Building the plan checks every segment once; `launch()` then costs one C call, which keeps
+    the host far ahead of the GPU when the same assembly is replayed. The plan keeps references
+    to its tensors so their memory stays valid.
+
+    segments: iterable of (K, V, delta, dst_tok0); K, V contiguous CUDA tensors whose leading
+      dims flatten to the same (layers * kv_heads) as the outputs, shape [..., n, D].
+    out_k, out_v: contiguous [..., T_out, D] CUDA tensors of the same dtype.
+    inv_freq: D/2 fp32 inverse frequencies (host list or tensor).
+    """
+
+    def __init__(self, segments, out_k, out_v, inv_freq, attn_scaling=1.0):
+        segs = list(segments)
+        for t, nm in ((out_k, "out_k"), (out_v, "out_v")):
+            C.require_cuda(t, nm)
+            if not t.is_contiguous():
+                raise ValueError(f"{nm} must be contiguous")
+        if out_k.shape != out_v.shape or out_k.dtype != out_v.dtype:
+            raise ValueError("out_k and out_v must have the same shape and dtype")
+        D = out_k.shape[-1]
+        T_out = out_k.shape[-2]
+        LH = out_k.numel() // (T_out * D) if T_out * D else 0
+        kp, vp, n, dl, d0 = [], [], [], [], []
+        for K, V, delta, dst0 in segs:
+            nk, dk = _flat_kv(K, "K")
+            _flat_kv(V, "V")
+            if K.shape != V.shape or dk != D or K.numel() != LH * nk * D:
+                raise ValueError(f"segment K/V shape {tuple(K.shape)} does not match output {tuple(out_k.shape)}")
+            if K.dtype != out_k.dtype or V.dtype != out_k.dtype:
+                raise TypeError("segment dtype differs from the output dtype")
+            if K.device != out_k.device or V.device != out_k.device:
+                raise ValueError("segment and output on different devices")
+            kp.append(K.data_ptr())
+            vp.append(V.data_ptr())
+            n.append(nk)
+            dl.append(int(delta))
+            d0.append(int(dst0))
+        inv = inv_freq.tolist() if isinstance(inv_freq, torch.Tensor) else [float(x) for x in inv_freq]
+        if len(inv) != D // 2:
+            raise ValueError(f"inv_freq has {len(inv)} entries, expected {D // 2}")
+        self.device = out_k.device
+        self.nseg = len(segs)
+        self._keep = (segs, out_k, out_v)
+        self._args = (C.ptr_array(kp), C.ptr_array(vp), C.i32_array(n), C.i64_array(dl), C.i64_array(d0),
+                      len(segs), out_k.data_ptr(), out_v.data_ptr(), LH, 1, D, T_out, C.f32_array(inv),
+                      float(attn_scaling), C.dtype_code(out_k.dtype))
+
+    def launch(self, stream=None):
+        if self.nseg == 0:
+            return
+        st = C.stream_ptr(self.device) if stream is None else C.P(stream.cuda_stream)
+        rc = C.lib().tread_rope_gather_append(*self._args, st)
+        C.check(rc, "tread_rope_gather_append")
+
+
+def rope_gather_append(segments, out_k, out_v, inv_freq, attn_scaling=1.0, stream=None):
+    """Assemble cached blocks into out_k/out_v with RoPE re-rotation of K (one launch).
+    See RopeAppendPlan for the argument layout."""
+    RopeAppendPlan(segments, out_k, out_v, inv_freq, attn_scaling).launch(stream)
+    return out_k, out_v
+
+
+def _stream_arg(stream, device):
+    if stream is None:
+        return C.stream_ptr(device)
+    return C.P(stream.cuda_stream)
+
+
+def kv_fetch(dst, src, stream=None):
+    """Pinned host tensor `src` -> device tensor `dst` (same byte size), async on `stream`."""
+    C.require_cuda(dst, "dst")
+    if src.is_cuda or not src.is_pinned():
+        raise ValueError("kv_fetch source must be a pinned (page-locked) CPU tensor")
+    if not (dst.is_contiguous() and src.is_contiguous()) or dst.nbytes != src.nbytes:
+        raise ValueError("kv_fetch needs contiguous tensors of equal byte size")
+    with torch.cuda.device(dst.device):
+        C.check(C.lib().tread_kv_fetch(dst.data_ptr(), src.data_ptr(), dst.nbytes, _stream_arg(stream, dst.device)),
+                "tread_kv_fetch")
+
+
+def kv_spill(dst, src, stream=None):
+    """Device tensor `src` -> pinned host tensor `dst` (same byte size), async on `stream`."""
+    C.require_cuda(src, "src")
+    if dst.is_cuda or not dst.is_pinned():
+        raise ValueError("kv_spill destination must be a pinned (page-locked) CPU tensor")
+    if not (dst.is_contiguous() and src.is_contiguous()) or dst.nbytes != src.nbytes:
+        raise ValueError("kv_spill needs contiguous tensors of equal byte size")
+    with torch.cuda.device(src.device):
+        C.check(C.lib().tread_kv_spill(dst.data_ptr(), src.data_ptr(), src.nbytes, _stream_arg(stream, src.device)),
+                "tread_kv_spill")
+
+
+def _rows(t, tok0, n):
+    """(base pointer, pitch, row bytes, rows) of tokens [tok0, tok0+n) of a [..., T, D] tensor."""
+    T, D = t.shape[-2], t.shape[-1]
+    es = t.element_size()
+    return t.data_ptr() + tok0 * D * es, T * D * es, n * D * es, t.numel() // (T * D)
+
+
+def kv_spill_rows(dst_host, src_dev, tok0, n, stream=None):
+    """Copy tokens [tok0, tok0+n) of every (layer, head) row of a device [..., T, D] cache into the
+    same tokens of a pinned host tensor of the same shape."""
+    C.require_cuda(src_dev, "src")
+    if dst_host.is_cuda or not dst_host.is_pinned() or dst_host.shape != src_dev.shape:
+        raise ValueError("kv_spill_rows needs a pinned host tensor of the source's shape")
+    if not (dst_host.is_contiguous() and src_dev.is_contiguous()) or tok0 < 0 or tok0 + n > src_dev.shape[-2]:
+        raise ValueError("kv_spill_rows: bad token range or non-contiguous tensors")
+    d, pitch, rb, rows = _rows(dst_host, tok0, n)
+    s, _, _, _ = _rows(src_dev, tok0, n)
+    with torch.cuda.device(src_dev.device):
+        C.check(C.lib().tread_kv_spill_rows(d, pitch, s, pitch, rb, rows, _stream_arg(stream, src_dev.device)),
+                "tread_kv_spill_rows")
