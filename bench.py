@@ -46,7 +46,9 @@ def parse():
     ap.add_argument("--impl", default="tread_b200", choices=["tread_b200", "reference"])
     ap.add_argument("--pool", type=int, default=64)
     ap.add_argument("--blocks", type=int, default=16)
-    ap.add_argument("--e2e-steps", type=int, default=5)
+    ap.add_argument("--e2e-steps", type=int, default=5, help="0 skips the host-buffer (e2e) leg")
+    ap.add_argument("--settle", type=float, default=1.0,
+                    help="seconds of untimed launches before warm-up so the clock record sees a loaded GPU")
     ap.add_argument("--seed", type=int, default=0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=10.0, help="CPU baseline sample budget")
@@ -258,7 +260,7 @@ def run_gpu(args):
     # settle: ~1 s of untimed work so the clock record covers a loaded GPU even for small --steps
     t_settle = time.perf_counter()
     s = 0
-    while time.perf_counter() - t_settle < 1.0:
+    while time.perf_counter() - t_settle < args.settle:
         plans[s % len(plans)].launch(stream)
         s += 1
         if s % 64 == 0:
@@ -289,7 +291,8 @@ def run_gpu(args):
     kern_ms_max = max_over_ranks(kern_ms, world, dev)
     clk = clocks.stop(t_wall0 - 1.5, t_wall1 + 0.2) if clocks else None
 
-    e2e = run_e2e(args, dev, pool_k, pool_v, ids, deltas, inv, world, rank)
+    e2e = run_e2e(args, dev, pool_k, pool_v, ids, deltas, inv, world, rank) if args.e2e_steps > 0 else None
+    selector = run_selector(args, dev, out_k, out_v, world)
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
@@ -312,6 +315,7 @@ def run_gpu(args):
                          "bytes_per_launch": nbytes, "traffic": TRAFFIC_PER_LAUNCH},
             "cpu_baseline": cpu,
             "e2e": e2e,
+            "selector": selector,
             "gpu_launches": args.steps,
             "clocks": clk,
         }
@@ -323,9 +327,45 @@ def run_gpu(args):
     return 0
 
 
-# dram__bytes_read.sum + dram__bytes_write.sum of one launch from an ncu capture of this kernel
-# (profiles/rope_gather_append_cfg2.md); None until captured.
-TRAFFIC_PER_LAUNCH = None
+# dram__bytes_read.sum + dram__bytes_write.sum of one launch of this kernel on this workload from an
+# ncu --set full capture (profiles/rope_gather_append_cfg2.md): 469.76 MB read + 421.91 MB written.
+TRAFFIC_PER_LAUNCH = 469762048 + 421905920
+
+
+def run_selector(args, dev, out_k, out_v, world):
+    """Deviation + top-k on the assembled cache: fresh layer-1 rows for all
+    8192 tokens against layer 1 of the cache, budget 20% (1638). Reads 33.6 MB per call."""
+    from tread_b200 import kernels
+
+    T = out_k.shape[-2]
+    gen = torch.Generator(device=dev).manual_seed(5)
+    K1, V1 = out_k[1, 0], out_v[1, 0]  # [Hkv, T, D] layer-1 views
+    k1 = (K1.float() + 0.05 * torch.randn(K1.shape, generator=gen, device=dev)).to(torch.bfloat16)
+    v1 = (V1.float() + 0.05 * torch.randn(V1.shape, generator=gen, device=dev)).to(torch.bfloat16)
+    pos = torch.arange(T, device=dev)
+    budget = int(round(0.2 * T))
+    ws = kernels.workspace(dev)
+    devb = torch.empty(T, dtype=torch.float32, device=dev)
+    sel = torch.empty(budget, dtype=torch.int64, device=dev)
+    spos = torch.empty(budget, dtype=torch.int64, device=dev)
+    for _ in range(5):
+        kernels.deviation_topk(k1, v1, K1, V1, pos, budget, devb, sel, spos, ws)
+    nrep = 50
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(nrep)]
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)  # 2x L2: evicts the inputs between calls
+    torch.cuda.synchronize(dev)
+    for a, b in ev:
+        flush.zero_()
+        a.record()
+        kernels.deviation_topk(k1, v1, K1, V1, pos, budget, devb, sel, spos, ws)
+        b.record()
+    torch.cuda.synchronize(dev)
+    us = statistics.median(a.elapsed_time(b) for a, b in ev) * 1e3
+    us = max_over_ranks(us, world, dev)
+    nbytes = 4 * HKV * T * D * 2
+    return {"kernel": "deviation_topk_kernel<bf16>", "n": T, "budget": budget, "us_per_call": round(us, 2),
+            "read_bytes": nbytes, "gbs": round(nbytes / (us * 1e-6) / 1e9, 1),
+            "note": "L2 flushed (256 MB write) before each call; median of 50 calls"}
 
 
 def load_peaks():

@@ -74,6 +74,37 @@ int tread_rope_gather_append(const void* const* k_src, const void* const* v_src,
                              float attn_scaling, int dtype, tread_stream_t stream);
 
 /*
+ * Fused layer-1 KV deviation + top-k selection (CacheBlend-style token selector).
+ *
+ * Replaces tread/blend.py:129 (per-candidate deviation), :160 (dev.topk(budget)) and :165
+ * (S.sort()) in one launch:
+ *   dev[t] = sum_h ||k1[h,t] - K1[h,pos_t]||_2 + sum_h ||v1[h,t] - V1[h,pos_t]||_2
+ * in fp32 with a fixed summation order (per head: 32 lanes of D/32 consecutive elements
+ * accumulated in order, xor-butterfly 16,8,4,2,1, IEEE sqrt; heads summed in order; K sum
+ * plus V sum), then the `budget` largest dev values (ties -> lower candidate index) written
+ * as ascending candidate indices to sel_idx and their positions cand_pos[sel_idx] to sel_pos.
+ *
+ *   k1, v1     : fresh layer-1 rows; element (h, t, d) at t*fresh_stride_tok +
+ *                h*fresh_stride_head + d (elements)
+ *   K1, V1     : layer-1 assembled cache; element (h, p, d) at p*cache_stride_tok +
+ *                h*cache_stride_head + d; positions must lie in [0, T_cache)
+ *   cand_pos   : device int64 [n], candidate positions (tread's all_c)
+ *   D          : 64, 128 or 256; rows aligned to D/32 elements
+ *   dev_out    : device fp32 [n]; sel_idx, sel_pos : device int64 [budget] (sel_pos may be NULL)
+ *   workspace  : device buffer of TREAD_DEVIATION_WORKSPACE_BYTES, zero-filled once by the
+ *                caller; word 0 is a CTA ticket the kernel returns to zero, word 1 a sticky
+ *                flag set to 1 if a candidate position was out of range (that dev is NaN).
+ *                Calls sharing a workspace must be stream-ordered.
+ */
+#define TREAD_DEVIATION_WORKSPACE_BYTES 256
+int tread_deviation_topk(const void* k1, const void* v1, int64_t fresh_stride_tok,
+                         int64_t fresh_stride_head, const void* K1, const void* V1,
+                         int64_t cache_stride_tok, int64_t cache_stride_head, int64_t T_cache,
+                         const int64_t* cand_pos, int n, int Hkv, int D, int budget, int dtype,
+                         float* dev_out, int64_t* sel_idx, int64_t* sel_pos, void* workspace,
+                         tread_stream_t stream);
+
+/*
  * Block-store tier transfers (pinned host <-> HBM), stream-ordered DMA copies.
  *
  * tread_kv_spill replaces the GPU->CPU-tier move of tread/store.py:111

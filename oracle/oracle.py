@@ -43,6 +43,9 @@ def lib():
             ctypes.c_int, ctypes.c_int, ctypes.c_int]
         h.oracle_rope_gather_append.restype = None
         h.oracle_max_threads.restype = ctypes.c_int
+        h.oracle_deviation.argtypes = [P, P, ctypes.c_int64, ctypes.c_int64, P, P, ctypes.c_int64, ctypes.c_int64, P,
+                                       ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int, P]
+        h.oracle_deviation.restype = None
         _lib = h
     return _lib
 
@@ -132,3 +135,39 @@ def inv_freq(head_dim, theta):
     import torch
 
     return (1.0 / (theta ** (torch.arange(0, head_dim, 2, dtype=torch.int64).to(torch.float) / head_dim))).numpy()
+
+
+# ---- A4: deviation + selection (tread/blend.py:117-130, 145, 158-169) -----------------------
+
+def deviation(k1, v1, K1, V1, cand_pos):
+    """dev[t] in the kernel's fixed fp32 order. k1, v1: [H, n, D] fresh layer-1 rows; K1, V1:
+    [H, T, D] layer-1 cache; cand_pos: [n] positions. Arrays: float32 / float16 / uint16 (bf16)."""
+    k1, v1, K1, V1 = (np.ascontiguousarray(a) for a in (k1, v1, K1, V1))
+    H, n, D = k1.shape
+    T = K1.shape[1]
+    pos = np.ascontiguousarray(cand_pos, dtype=np.int64)
+    assert v1.shape == k1.shape and K1.shape == V1.shape == (H, T, D) and pos.shape == (n,)
+    assert ((pos >= 0) & (pos < T)).all()
+    dev = np.empty(n, np.float32)
+    lib().oracle_deviation(k1.ctypes.data, v1.ctypes.data, D, n * D, K1.ctypes.data, V1.ctypes.data, D, T * D,
+                           pos.ctypes.data, n, H, D, _np_code(k1), dev.ctypes.data)
+    return dev
+
+
+def order_key(dev):
+    """Order-preserving uint32 image of fp32 values (NaN above +inf, as torch.topk ranks it)."""
+    u = np.ascontiguousarray(dev, dtype=np.float32).view(np.uint32)
+    return np.where(u & 0x80000000, ~u, u | 0x80000000).astype(np.uint32)
+
+
+def select_topk(dev, budget):
+    """Indices of the `budget` largest values, ties toward the lower index, returned ascending
+    (the set sort(topk(dev, budget).indices), tread/blend.py:160,165)."""
+    key = order_key(dev).astype(np.int64)
+    order = np.argsort(-key, kind="stable")
+    return np.sort(order[:budget])
+
+
+def budget_for(ratio, n):
+    """tread/blend.py:145: int(round(ratio * n)) with Python's round-half-to-even."""
+    return int(round(ratio * n))

@@ -131,3 +131,49 @@ int oracle_max_threads(void) {
   return 1;
 #endif
 }
+
+/* ---- A4: layer-1 deviation (tread/blend.py:129) ---------------------------------------- */
+
+/*
+ * L2 norm of (x - y) over one D-row in the fixed order the CUDA kernel uses: 32 lanes own
+ * E = D/32 consecutive elements each and accumulate fl(p + fl(d*d)) in element order; the
+ * lane partials are combined by an xor butterfly with offsets 16, 8, 4, 2, 1; then sqrt.
+ */
+static float row_norm(const void* x, size_t xo, const void* y, size_t yo, int D, int dtype) {
+  const int E = D / 32;
+  float p[32], q[32];
+  for (int l = 0; l < 32; ++l) {
+    float acc = 0.f;
+    for (int e = 0; e < E; ++e) {
+      const float d = load_elem(x, xo + (size_t)l * E + e, dtype) - load_elem(y, yo + (size_t)l * E + e, dtype);
+      const float sq = d * d;
+      acc = acc + sq;
+    }
+    p[l] = acc;
+  }
+  for (int off = 16; off >= 1; off >>= 1) {
+    for (int l = 0; l < 32; ++l) q[l] = p[l] + p[l ^ off];
+    memcpy(p, q, sizeof(p));
+  }
+  return sqrtf(p[0]);
+}
+
+/*
+ * dev[t] = sum_h ||k1[h,t] - K1[h,pos_t]|| + sum_h ||v1[h,t] - V1[h,pos_t]||, heads summed in
+ * order, K sum + V sum last. Element (h, t, d) of the fresh rows is at t*f_st + h*f_sh + d,
+ * element (h, pos, d) of the cache at pos*c_st + h*c_sh + d.
+ */
+void oracle_deviation(const void* k1, const void* v1, int64_t f_st, int64_t f_sh, const void* K1, const void* V1,
+                      int64_t c_st, int64_t c_sh, const int64_t* cand_pos, int n, int H, int D, int dtype,
+                      float* dev) {
+  for (int t = 0; t < n; ++t) {
+    const int64_t pos = cand_pos[t];
+    float a = 0.f, b = 0.f;
+    for (int h = 0; h < H; ++h) {
+      const size_t fo = (size_t)(t * f_st + h * f_sh), co = (size_t)(pos * c_st + h * c_sh);
+      a = a + row_norm(k1, fo, K1, co, D, dtype);
+      b = b + row_norm(v1, fo, V1, co, D, dtype);
+    }
+    dev[t] = a + b;
+  }
+}

@@ -68,3 +68,33 @@ def test_rope_gather_append_rejects_bad_arguments(over, needle):
 def test_rope_gather_append_empty_is_noop():
     assert _rope_call(nseg=0) == 0
     assert _rope_call(n=[0]) == 0
+
+
+def _dev_call(**over):
+    a = dict(k1=256, v1=256, fst=128, fsh=1024, K1=256, V1=256, cst=128, csh=4096, T=32, pos=256, n=8, H=4,
+             D=128, budget=2, dtype=C.TREAD_BF16, dev=256, sel=256, spos=256, ws=256)
+    a.update(over)
+    return C.lib().tread_deviation_topk(a["k1"], a["v1"], a["fst"], a["fsh"], a["K1"], a["V1"], a["cst"], a["csh"],
+                                        a["T"], a["pos"], a["n"], a["H"], a["D"], a["budget"], a["dtype"], a["dev"],
+                                        a["sel"], a["spos"], a["ws"], None)
+
+
+@pytest.mark.parametrize("over,needle", [
+    (dict(budget=9), "budget"),
+    (dict(budget=-1), "budget"),
+    (dict(D=96), "D in"),
+    (dict(H=0), "Hkv"),
+    (dict(dtype=9), "dtype"),
+    (dict(k1=258), "aligned"),
+    (dict(fst=130), "multiples"),
+    (dict(ws=260), "workspace"),
+    (dict(T=0), "T_cache"),
+    (dict(sel=None), "sel_idx"),
+])
+def test_deviation_topk_rejects_bad_arguments(over, needle):
+    assert _dev_call(**over) == 1
+    assert needle in C.lib().tread_last_error().decode()
+
+
+def test_deviation_topk_empty_is_noop():
+    assert _dev_call(n=0, budget=0) == 0

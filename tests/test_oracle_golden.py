@@ -58,3 +58,27 @@ def test_oracle_assembly_places_segments(rope):
     np.testing.assert_allclose(ok[..., 2 * n:3 * n, :], rope["d64_rot_-1"], atol=3e-6 * 8)
     np.testing.assert_array_equal(ok[..., :n, :], orc.bf16_to_f32(kb))
     assert (ok[..., 3 * n:, :] == 0).all() and (ov[..., 3 * n:, :] == 0).all()
+
+
+def test_oracle_deviation_matches_reference_layer1_deviation():
+    """dev (tread/blend.py:129) restated in a fixed fp32 order agrees with the reference's torch
+    reduction to rounding, and selects the same set as the reference's topk."""
+    g = golden("deviation.npz")
+    k1, v1, K1g, V1g = g["k1"], g["v1"], g["K1"], g["V1"]  # [H, n, D]; K1g/V1g gathered at all_c
+    H, n, D = k1.shape
+    dev = orc.deviation(k1, v1, K1g, V1g, np.arange(n))
+    np.testing.assert_allclose(dev, g["dev"], rtol=2e-6, atol=0)
+    budget = int(g["budget"])
+    assert budget == orc.budget_for(0.2, n)
+    sel = orc.select_topk(dev, budget)
+    np.testing.assert_array_equal(sel, np.sort(g["topk"]))
+    np.testing.assert_array_equal(g["all_c"][sel], g["S"])
+
+
+def test_select_topk_tie_break_and_budget_rounding():
+    dev = np.array([1.0, 3.0, 3.0, 2.0, 3.0, 0.5], np.float32)
+    np.testing.assert_array_equal(orc.select_topk(dev, 2), [1, 2])
+    np.testing.assert_array_equal(orc.select_topk(dev, 4), [1, 2, 3, 4])
+    np.testing.assert_array_equal(orc.select_topk(dev, 6), np.arange(6))
+    assert orc.budget_for(0.5, 5) == 2 and orc.budget_for(0.5, 7) == 4  # banker's rounding, as Python round
+    assert orc.budget_for(0.2, 7936) == 1587 and orc.budget_for(0.2, 8192) == 1638

@@ -31,6 +31,11 @@ SIGNATURES = {
         [PP, PP, PI32, PI64, PI64, ctypes.c_int, P, P, ctypes.c_int, ctypes.c_int, ctypes.c_int, I64, PF32,
          F32, ctypes.c_int, P],
     ),
+    "tread_deviation_topk": (
+        ctypes.c_int,
+        [P, P, I64, I64, P, P, I64, I64, I64, P, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int,
+         ctypes.c_int, P, P, P, P, P],
+    ),
     "tread_kv_fetch": (ctypes.c_int, [P, P, ctypes.c_size_t, P]),
     "tread_kv_spill": (ctypes.c_int, [P, P, ctypes.c_size_t, P]),
     "tread_kv_fetch_rows": (ctypes.c_int, [P, ctypes.c_size_t, P, ctypes.c_size_t, ctypes.c_size_t,

@@ -1,0 +1,284 @@
+// Fused layer-1 KV deviation + deterministic top-k selection (sm_100a).
+//
+// Replaces tread/blend.py:129 (dev = Σ_h‖k1−K1[S]‖₂ + Σ_h‖v1−V1[S]‖₂, a chain of sub / norm /
+// sum kernels over gathered copies), :145/:160 (budget, torch.topk) and :165 (sort) with one
+// launch:
+//   phase 1  one warp per candidate reads the fresh and cached layer-1 rows of every KV head
+//            straight from their tensors (the cache rows gathered by position, no copy) and
+//            writes dev in fp32 with a fixed summation order (below);
+//   phase 2  the last CTA to finish (an atomic ticket in `workspace`) selects the `budget`
+//            largest dev values with an MSB-first radix select on order-preserving uint32 keys,
+//            breaks ties toward the lower candidate index, and compacts the selection in
+//            ascending index order. That is the set `S = sort(all_c[topk(dev, budget)])`.
+//
+// Fixed fp32 order (restated exactly by the CPU oracle, so selections compare bit-for-bit):
+//   lane l of the warp owns elements [l*E, (l+1)*E) of a D-row (E = D/32) and accumulates
+//   fl(p + fl(d*d)) in element order, d = fl(fresh - cached); lanes then combine by an xor
+//   butterfly with offsets 16, 8, 4, 2, 1; norm = sqrt (IEEE); per token
+//   a = (((n_k0 + n_k1) + n_k2) + ...), b likewise over V heads, dev = a + b.
+#include "common.cuh"
+
+namespace tread {
+namespace {
+
+constexpr int kThreads = 512;
+constexpr int kWarps = kThreads / 32;
+
+template <typename T, int E>
+__device__ __forceinline__ void load_row(const T* p, float (&x)[E]) {
+  if constexpr (E * sizeof(T) == 16) {
+    Vec16<T> v;
+    v.raw = __ldg(reinterpret_cast<const int4*>(p));
+#pragma unroll
+    for (int e = 0; e < E; ++e) x[e] = Num<T>::to_f(v.e[e]);
+  } else if constexpr (E * sizeof(T) == 8) {
+    union {
+      uint2 raw;
+      T e[E];
+    } v;
+    v.raw = __ldg(reinterpret_cast<const uint2*>(p));
+#pragma unroll
+    for (int e = 0; e < E; ++e) x[e] = Num<T>::to_f(v.e[e]);
+  } else {
+#pragma unroll
+    for (int e = 0; e < E; ++e) x[e] = Num<T>::to_f(p[e]);
+  }
+}
+
+template <int E>
+__device__ __forceinline__ float row_norm(const float (&a)[E], const float (&b)[E]) {
+  float p = 0.f;
+#pragma unroll
+  for (int e = 0; e < E; ++e) {
+    const float d = __fsub_rn(a[e], b[e]);
+    p = __fadd_rn(p, __fmul_rn(d, d));
+  }
+#pragma unroll
+  for (int off = 16; off >= 1; off >>= 1) p = __fadd_rn(p, __shfl_xor_sync(0xffffffffu, p, off));
+  return __fsqrt_rn(p);
+}
+
+__device__ __forceinline__ unsigned order_key(float f) {
+  const unsigned u = __float_as_uint(f);
+  return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+}
+
+// Exclusive block scan of a 0/1 flag; returns the prefix and writes the block total.
+__device__ __forceinline__ unsigned block_scan(bool flag, unsigned* s_warp, unsigned& total) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const unsigned bal = __ballot_sync(0xffffffffu, flag);
+  const unsigned in_warp = __popc(bal & ((1u << lane) - 1u));
+  if (lane == 0) s_warp[warp] = __popc(bal);
+  __syncthreads();
+  if (warp == 0) {
+    unsigned v = lane < kWarps ? s_warp[lane] : 0u;
+    unsigned incl = v;
+#pragma unroll
+    for (int off = 1; off < 32; off <<= 1) {
+      const unsigned o = __shfl_up_sync(0xffffffffu, incl, off);
+      if (lane >= off) incl += o;
+    }
+    if (lane < kWarps) s_warp[lane] = incl - v;  // exclusive warp offsets
+    if (lane == kWarps - 1) s_warp[kWarps] = incl;
+  }
+  __syncthreads();
+  const unsigned r = s_warp[warp] + in_warp;
+  total = s_warp[kWarps];
+  __syncthreads();
+  return r;
+}
+
+// Top-`budget` of dev[0..n) (largest first, lower index wins ties), written ascending by index.
+__device__ void select_topk(const float* dev, int n, int budget, const int64_t* cand_pos, int64_t* sel_idx,
+                            int64_t* sel_pos) {
+  __shared__ unsigned hist[256];
+  __shared__ unsigned s_warp[kWarps + 1];
+  __shared__ unsigned s_digit, s_rem;
+  const int tid = threadIdx.x;
+  unsigned prefix = 0u, mask = 0u, remaining = (unsigned)budget;
+#pragma unroll 1
+  for (int shift = 24; shift >= 0; shift -= 8) {
+    for (int i = tid; i < 256; i += kThreads) hist[i] = 0u;
+    __syncthreads();
+    for (int i = tid; i < n; i += kThreads) {
+      const unsigned key = order_key(__ldcg(dev + i));
+      if ((key & mask) == prefix) atomicAdd(&hist[(key >> shift) & 255u], 1u);
+    }
+    __syncthreads();
+    if (tid < 32) {
+      // warp 0: find the digit holding the `remaining`-th largest key, scanning from 255 down
+      unsigned cum = 0u;
+      int found = -1;
+      unsigned rem_out = 0u;
+#pragma unroll 1
+      for (int chunk = 7; chunk >= 0 && found < 0; --chunk) {
+        const int d = chunk * 32 + (31 - tid);  // lane 0 holds the highest digit of the chunk
+        const unsigned c = hist[d];
+        unsigned incl = c;  // inclusive count over higher digits within the chunk
+#pragma unroll
+        for (int off = 1; off < 32; off <<= 1) {
+          const unsigned o = __shfl_up_sync(0xffffffffu, incl, off);
+          if (tid >= off) incl += o;
+        }
+        const bool hit = cum + incl >= remaining && cum + incl - c < remaining;
+        const unsigned b = __ballot_sync(0xffffffffu, hit);
+        if (b) {
+          const int src = __ffs(b) - 1;
+          const unsigned above = __shfl_sync(0xffffffffu, cum + incl - c, src);
+          found = chunk * 32 + (31 - src);
+          rem_out = remaining - above;
+        }
+        cum += __shfl_sync(0xffffffffu, incl, 31);
+      }
+      if (tid == 0) {
+        s_digit = (unsigned)found;
+        s_rem = rem_out;
+      }
+    }
+    __syncthreads();
+    prefix |= s_digit << shift;
+    mask |= 255u << shift;
+    remaining = s_rem;
+    __syncthreads();
+  }
+  // prefix is the key of the budget-th largest value; `remaining` of its ties are taken,
+  // lowest indices first.
+  unsigned eq_base = 0u, sel_base = 0u;
+#pragma unroll 1
+  for (int base = 0; base < n; base += kThreads) {
+    const int i = base + tid;
+    const unsigned key = i < n ? order_key(__ldcg(dev + i)) : 0u;
+    const bool gt = i < n && key > prefix;
+    const bool eq = i < n && key == prefix;
+    unsigned teq, tsel;
+    const unsigned eq_rank = eq_base + block_scan(eq, s_warp, teq);
+    const bool sel = gt || (eq && eq_rank < remaining);
+    const unsigned r = sel_base + block_scan(sel, s_warp, tsel);
+    if (sel) {
+      sel_idx[r] = i;
+      if (sel_pos) sel_pos[r] = cand_pos[i];
+    }
+    eq_base += teq;
+    sel_base += tsel;
+  }
+}
+
+template <typename T, int E>
+__global__ void __launch_bounds__(kThreads)
+    deviation_topk_kernel(const T* __restrict__ k1, const T* __restrict__ v1, long long f_st, long long f_sh,
+                          const T* __restrict__ K1, const T* __restrict__ V1, long long c_st, long long c_sh,
+                          long long T_cache, const int64_t* __restrict__ cand_pos, int n, int H, int budget,
+                          float* __restrict__ dev_out, int64_t* __restrict__ sel_idx, int64_t* __restrict__ sel_pos,
+                          unsigned* __restrict__ workspace) {
+  const int lane = threadIdx.x & 31;
+  const int t = blockIdx.x * kWarps + (threadIdx.x >> 5);
+  if (t < n) {
+    const long long pos = cand_pos[t];
+    float dev;
+    if (pos < 0 || pos >= T_cache) {
+      if (lane == 0) atomicOr(workspace + 1, 1u);  // sticky error flag for the caller
+      dev = __int_as_float(0x7fc00000);
+    } else {
+      float a = 0.f, b = 0.f;
+#pragma unroll 1
+      for (int h = 0; h < H; ++h) {
+        float fk[E], ck[E], fv[E], cv[E];
+        const long long fo = (long long)t * f_st + (long long)h * f_sh + lane * E;
+        const long long co = pos * c_st + (long long)h * c_sh + lane * E;
+        load_row<T, E>(k1 + fo, fk);
+        load_row<T, E>(K1 + co, ck);
+        load_row<T, E>(v1 + fo, fv);
+        load_row<T, E>(V1 + co, cv);
+        a = __fadd_rn(a, row_norm<E>(fk, ck));
+        b = __fadd_rn(b, row_norm<E>(fv, cv));
+      }
+      dev = __fadd_rn(a, b);
+    }
+    if (lane == 0) dev_out[t] = dev;
+  }
+  if (budget <= 0) return;
+  __shared__ bool s_last;
+  __threadfence();
+  __syncthreads();
+  if (threadIdx.x == 0) s_last = atomicAdd(workspace, 1u) == gridDim.x - 1;
+  __syncthreads();
+  if (!s_last) return;
+  __threadfence();
+  select_topk(dev_out, n, budget, cand_pos, sel_idx, sel_pos);
+  if (threadIdx.x == 0) workspace[0] = 0u;  // ready for the next call
+}
+
+template <typename T, int E>
+int launch_dev(const void* k1, const void* v1, long long f_st, long long f_sh, const void* K1, const void* V1,
+               long long c_st, long long c_sh, long long T_cache, const int64_t* cand_pos, int n, int H, int budget,
+               float* dev_out, int64_t* sel_idx, int64_t* sel_pos, unsigned* ws, cudaStream_t st) {
+  const int grid = (n + kWarps - 1) / kWarps;
+  deviation_topk_kernel<T, E><<<grid, kThreads, 0, st>>>(
+      static_cast<const T*>(k1), static_cast<const T*>(v1), f_st, f_sh, static_cast<const T*>(K1),
+      static_cast<const T*>(V1), c_st, c_sh, T_cache, cand_pos, n, H, budget, dev_out, sel_idx, sel_pos, ws);
+  TREAD_CHECK_LAUNCH("deviation_topk_kernel");
+  return TREAD_OK;
+}
+
+template <typename T>
+int dispatch_e(int D, const void* k1, const void* v1, long long f_st, long long f_sh, const void* K1,
+               const void* V1, long long c_st, long long c_sh, long long T_cache, const int64_t* cand_pos, int n,
+               int H, int budget, float* dev_out, int64_t* sel_idx, int64_t* sel_pos, unsigned* ws, cudaStream_t st) {
+  switch (D) {
+    case 64:
+      return launch_dev<T, 2>(k1, v1, f_st, f_sh, K1, V1, c_st, c_sh, T_cache, cand_pos, n, H, budget, dev_out,
+                              sel_idx, sel_pos, ws, st);
+    case 128:
+      return launch_dev<T, 4>(k1, v1, f_st, f_sh, K1, V1, c_st, c_sh, T_cache, cand_pos, n, H, budget, dev_out,
+                              sel_idx, sel_pos, ws, st);
+    default:
+      return launch_dev<T, 8>(k1, v1, f_st, f_sh, K1, V1, c_st, c_sh, T_cache, cand_pos, n, H, budget, dev_out,
+                              sel_idx, sel_pos, ws, st);
+  }
+}
+
+}  // namespace
+}  // namespace tread
+
+extern "C" int tread_deviation_topk(const void* k1, const void* v1, int64_t fresh_stride_tok,
+                                    int64_t fresh_stride_head, const void* K1, const void* V1,
+                                    int64_t cache_stride_tok, int64_t cache_stride_head, int64_t T_cache,
+                                    const int64_t* cand_pos, int n, int Hkv, int D, int budget, int dtype,
+                                    float* dev_out, int64_t* sel_idx, int64_t* sel_pos, void* workspace,
+                                    tread_stream_t stream) {
+  using namespace tread;
+  TREAD_CHECK_ARG(n >= 0 && budget >= 0 && budget <= n, "deviation_topk: need 0 <= budget (%d) <= n (%d)", budget,
+                  n);
+  if (n == 0) return TREAD_OK;
+  TREAD_CHECK_ARG(k1 && v1 && K1 && V1 && cand_pos && dev_out && workspace, "deviation_topk: null pointer");
+  TREAD_CHECK_ARG(budget == 0 || sel_idx, "deviation_topk: sel_idx is null");
+  TREAD_CHECK_ARG(Hkv > 0 && (D == 64 || D == 128 || D == 256), "deviation_topk: need Hkv > 0 and D in {64,128,256}");
+  const size_t es = dtype_size(dtype);
+  TREAD_CHECK_ARG(es != 0, "deviation_topk: unknown dtype %d", dtype);
+  const int E = D / 32;
+  const size_t vec_bytes = E * es;
+  auto al = [&](const void* p) { return (reinterpret_cast<uintptr_t>(p) % vec_bytes) == 0; };
+  TREAD_CHECK_ARG(al(k1) && al(v1) && al(K1) && al(V1), "deviation_topk: row pointers not %zu-byte aligned",
+                  vec_bytes);
+  TREAD_CHECK_ARG(fresh_stride_tok % E == 0 && fresh_stride_head % E == 0 && cache_stride_tok % E == 0 &&
+                      cache_stride_head % E == 0,
+                  "deviation_topk: strides must be multiples of D/32");
+  TREAD_CHECK_ARG(T_cache > 0, "deviation_topk: T_cache must be > 0");
+  TREAD_CHECK_ARG((reinterpret_cast<uintptr_t>(workspace) & 15u) == 0, "deviation_topk: workspace not aligned");
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  unsigned* ws = static_cast<unsigned*>(workspace);
+  switch (dtype) {
+    case TREAD_BF16:
+      return dispatch_e<__nv_bfloat16>(D, k1, v1, fresh_stride_tok, fresh_stride_head, K1, V1, cache_stride_tok,
+                                       cache_stride_head, T_cache, cand_pos, n, Hkv, budget, dev_out, sel_idx,
+                                       sel_pos, ws, st);
+    case TREAD_F16:
+      return dispatch_e<__half>(D, k1, v1, fresh_stride_tok, fresh_stride_head, K1, V1, cache_stride_tok,
+                                cache_stride_head, T_cache, cand_pos, n, Hkv, budget, dev_out, sel_idx, sel_pos, ws,
+                                st);
+    default:
+      return dispatch_e<float>(D, k1, v1, fresh_stride_tok, fresh_stride_head, K1, V1, cache_stride_tok,
+                               cache_stride_head, T_cache, cand_pos, n, Hkv, budget, dev_out, sel_idx, sel_pos, ws,
+                               st);
+  }
+}

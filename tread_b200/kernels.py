@@ -130,3 +130,79 @@ def kv_spill_rows(dst_host, src_dev, tok0, n, stream=None):
     with torch.cuda.device(src_dev.device):
         C.check(C.lib().tread_kv_spill_rows(d, pitch, s, pitch, rb, rows, _stream_arg(stream, src_dev.device)),
                 "tread_kv_spill_rows")
+
+
+# ---- deviation + top-k ----------------------------------------------------------------------
+
+WORKSPACE_BYTES = 256
+_workspaces = {}
+
+
+def workspace(device, stream=None):
+    """Zeroed scratch for tread_deviation_topk, one per (device, stream): calls that share one
+    must be ordered (the kernel's last CTA resets the ticket counter for the next call)."""
+    key = (torch.device(device).index, None if stream is None else stream.cuda_stream)
+    ws = _workspaces.get(key)
+    if ws is None:
+        ws = torch.zeros(WORKSPACE_BYTES // 4, dtype=torch.int32, device=device)
+        _workspaces[key] = ws
+    return ws
+
+
+def _rows_view(t, name):
+    """(tensor, token stride, head stride) of a [H, n, D] or [1, H, n, D] view with unit last stride."""
+    C.require_cuda(t, name)
+    if t.dim() == 4:
+        if t.shape[0] != 1:
+            raise ValueError(f"{name}: leading dim must be 1")
+        t = t[0]
+    if t.dim() != 3 or t.stride(-1) != 1:
+        raise ValueError(f"{name} must be [H, n, D] with contiguous rows")
+    return t, t.stride(1), t.stride(0)
+
+
+def deviation_topk(k1, v1, K1, V1, cand_pos, budget, dev_out=None, sel_idx=None, sel_pos=None, ws=None,
+                   stream=None):
+    """Layer-1 KV deviation of every candidate and the top-`budget` selection.
+
+    k1, v1: fresh layer-1 K/V rows of the candidates, [H, n, D] (or [1, H, n, D]) views;
+    K1, V1: the layer-1 assembled cache [H, T, D] (or [1, H, T, D]);
+    cand_pos: int64 CUDA tensor [n], cache position of each candidate.
+    Returns (dev fp32 [n], sel_idx int64 [budget] ascending candidate indices,
+             sel_pos int64 [budget] = cand_pos[sel_idx]).
+    """
+    k1, f_st, f_sh = _rows_view(k1, "k1")
+    v1, f_st2, f_sh2 = _rows_view(v1, "v1")
+    K1, c_st, c_sh = _rows_view(K1, "K1")
+    V1, c_st2, c_sh2 = _rows_view(V1, "V1")
+    if (f_st, f_sh) != (f_st2, f_sh2) or (c_st, c_sh) != (c_st2, c_sh2):
+        raise ValueError("k1/v1 (and K1/V1) must share strides")
+    H, n, D = k1.shape
+    if v1.shape != k1.shape or K1.shape[0] != H or K1.shape[2] != D or V1.shape != K1.shape:
+        raise ValueError("shape mismatch between fresh rows and cache")
+    if not (k1.dtype == v1.dtype == K1.dtype == V1.dtype):
+        raise TypeError("k1, v1, K1, V1 must share a dtype")
+    if cand_pos.dtype != torch.int64 or not cand_pos.is_cuda or cand_pos.numel() != n or not cand_pos.is_contiguous():
+        raise ValueError("cand_pos must be a contiguous int64 CUDA tensor of length n")
+    budget = int(budget)
+    if not 0 <= budget <= n:
+        raise ValueError(f"budget {budget} outside [0, {n}]")
+    dev = k1.device
+    if dev_out is None:
+        dev_out = torch.empty(n, dtype=torch.float32, device=dev)
+    if sel_idx is None:
+        sel_idx = torch.empty(budget, dtype=torch.int64, device=dev)
+    if sel_pos is None:
+        sel_pos = torch.empty(budget, dtype=torch.int64, device=dev)
+    if ws is None:
+        ws = workspace(dev, stream)
+    if n == 0:
+        return dev_out, sel_idx, sel_pos
+    with torch.cuda.device(dev):
+        rc = C.lib().tread_deviation_topk(
+            k1.data_ptr(), v1.data_ptr(), f_st, f_sh, K1.data_ptr(), V1.data_ptr(), c_st, c_sh, K1.shape[1],
+            cand_pos.data_ptr(), n, H, D, budget, C.dtype_code(k1.dtype), dev_out.data_ptr(),
+            sel_idx.data_ptr() if budget else None, sel_pos.data_ptr() if budget else None, ws.data_ptr(),
+            _stream_arg(stream, dev))
+    C.check(rc, "tread_deviation_topk")
+    return dev_out, sel_idx, sel_pos
