@@ -105,6 +105,42 @@ int tread_deviation_topk(const void* k1, const void* v1, int64_t fresh_stride_to
                          tread_stream_t stream);
 
 /*
+ * RoPE at each row's absolute position + splice of the row's K/V into the layer cache.
+ *
+ * Replaces, per recomputed layer, tread/blend.py:82-90 (`_qkv`: q/k/v views of the
+ * projections and apply_rotary_pos_emb at positions S) and tread/blend.py:106
+ * (`K[:, :, S], V[:, :, S] = k, v`). Row r of `qkv` ([R, ld_qkv], columns [q heads | k heads
+ * | v heads] of D each) sits at position pos[r]:
+ *   q_out[r, h, :]            = rope(q_h, pos[r])          (q_out: [R, Hq, D] contiguous)
+ *   K_cache[g*cs + pos[r]*D]  = rope(k_g, pos[r]);  V_cache[...] = v_g
+ * with cos/sin(float(pos) * inv_freq[i]) * attn_scaling in fp32, rounded once to `dtype`.
+ * The caches are one layer's [Hkv, T_cache, D] with head stride cache_stride_head (elements).
+ * A position outside [0, T_cache) skips its row and sets bit 0 of *err_flag (may be NULL).
+ * kv_by_row = 1 writes row r's k/v to cache row r instead of row pos[r] (dense [Hkv, R, D]
+ * outputs, e.g. the fresh layer-1 rows of the deviation selector, blend.py:128); q_out may be
+ * NULL to skip the q heads.
+ */
+int tread_rope_rows(const void* qkv, int64_t ld_qkv, const int64_t* pos, int R, int Hq, int Hkv, int D,
+                    void* q_out, void* K_cache, void* V_cache, int64_t cache_stride_head,
+                    int64_t T_cache, int kv_by_row, const float* inv_freq, float attn_scaling,
+                    int dtype, void* err_flag, tread_stream_t stream);
+
+/*
+ * Recompute attention: each row attends, per query head, to every cache key at a position
+ * <= its own, with GQA (query head h reads KV head h / (Hq/Hkv)).
+ *
+ * Replaces tread/blend.py:76 (mask[s, t] = t <= S[s]) and tread/blend.py:110
+ * (F.scaled_dot_product_attention(q, repeat_kv(K, g), repeat_kv(V, g), attn_mask=mask)),
+ * and, with the query segment's rows appended, the query forward's attention
+ * (tread/engine.py:131-132). q, out: [R, Hq, D]; K/V: one layer's [Hkv, T_cache, D] at head
+ * stride cache_stride_head; softmax in fp32 with scores scaled by sm_scale. Positions outside
+ * [0, T_cache) skip their row and set bit 1 of *err_flag (may be NULL).
+ */
+int tread_attn_rows(const void* q, const void* K_cache, const void* V_cache, int64_t cache_stride_head,
+                    int64_t T_cache, const int64_t* q_pos, int R, int Hq, int Hkv, int D, float sm_scale,
+                    void* out, int dtype, void* err_flag, tread_stream_t stream);
+
+/*
  * Block-store tier transfers (pinned host <-> HBM), stream-ordered DMA copies.
  *
  * tread_kv_spill replaces the GPU->CPU-tier move of tread/store.py:111

@@ -58,81 +58,85 @@ __device__ __forceinline__ float row_norm(const float (&a)[E], const float (&b)[
   return __fsqrt_rn(p);
 }
 
+// Order-preserving uint32 image of an fp32 value; every NaN maps to the top key (torch.topk
+// ranks NaN above +inf).
 __device__ __forceinline__ unsigned order_key(float f) {
   const unsigned u = __float_as_uint(f);
+  if ((u & 0x7fffffffu) > 0x7f800000u) return 0xffffffffu;
   return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
 }
 
-// Exclusive block scan of a 0/1 flag; returns the prefix and writes the block total.
-__device__ __forceinline__ unsigned block_scan(bool flag, unsigned* s_warp, unsigned& total) {
+// Exclusive block-wide prefix sum of one value per thread; `total` receives the block sum.
+__device__ __forceinline__ unsigned block_exclusive_sum(unsigned v, unsigned* s_scan, unsigned& total) {
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  const unsigned bal = __ballot_sync(0xffffffffu, flag);
-  const unsigned in_warp = __popc(bal & ((1u << lane) - 1u));
-  if (lane == 0) s_warp[warp] = __popc(bal);
+  unsigned incl = v;
+#pragma unroll
+  for (int off = 1; off < 32; off <<= 1) {
+    const unsigned o = __shfl_up_sync(0xffffffffu, incl, off);
+    if (lane >= off) incl += o;
+  }
+  if (lane == 31) s_scan[warp] = incl;
   __syncthreads();
   if (warp == 0) {
-    unsigned v = lane < kWarps ? s_warp[lane] : 0u;
-    unsigned incl = v;
+    const unsigned w = lane < kWarps ? s_scan[lane] : 0u;
+    unsigned wi = w;
 #pragma unroll
     for (int off = 1; off < 32; off <<= 1) {
-      const unsigned o = __shfl_up_sync(0xffffffffu, incl, off);
-      if (lane >= off) incl += o;
+      const unsigned o = __shfl_up_sync(0xffffffffu, wi, off);
+      if (lane >= off) wi += o;
     }
-    if (lane < kWarps) s_warp[lane] = incl - v;  // exclusive warp offsets
-    if (lane == kWarps - 1) s_warp[kWarps] = incl;
+    if (lane < kWarps) s_scan[lane] = wi - w;
+    if (lane == kWarps - 1) s_scan[kWarps] = wi;
   }
   __syncthreads();
-  const unsigned r = s_warp[warp] + in_warp;
-  total = s_warp[kWarps];
+  const unsigned r = s_scan[warp] + incl - v;
+  total = s_scan[kWarps];
   __syncthreads();
   return r;
 }
 
 // Top-`budget` of dev[0..n) (largest first, lower index wins ties), written ascending by index.
+// Thread t owns the contiguous index chunk [t*C, (t+1)*C): MSB-first radix select over 8-bit
+// digits (histogram, then a suffix scan over the 256 bins by threads 0..255), then one pass of
+// per-chunk counts and two block scans place every selected index.
 __device__ void select_topk(const float* dev, int n, int budget, const int64_t* cand_pos, int64_t* sel_idx,
                             int64_t* sel_pos) {
   __shared__ unsigned hist[256];
-  __shared__ unsigned s_warp[kWarps + 1];
+  __shared__ unsigned s_scan[kWarps + 1];
   __shared__ unsigned s_digit, s_rem;
-  const int tid = threadIdx.x;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int C = (n + kThreads - 1) / kThreads;
+  const int lo = min(n, tid * C), hi = min(n, lo + C);
   unsigned prefix = 0u, mask = 0u, remaining = (unsigned)budget;
 #pragma unroll 1
   for (int shift = 24; shift >= 0; shift -= 8) {
-    for (int i = tid; i < 256; i += kThreads) hist[i] = 0u;
+    if (tid < 256) hist[tid] = 0u;
     __syncthreads();
-    for (int i = tid; i < n; i += kThreads) {
+    for (int i = lo; i < hi; ++i) {
       const unsigned key = order_key(__ldcg(dev + i));
       if ((key & mask) == prefix) atomicAdd(&hist[(key >> shift) & 255u], 1u);
     }
     __syncthreads();
-    if (tid < 32) {
-      // warp 0: find the digit holding the `remaining`-th largest key, scanning from 255 down
-      unsigned cum = 0u;
-      int found = -1;
-      unsigned rem_out = 0u;
-#pragma unroll 1
-      for (int chunk = 7; chunk >= 0 && found < 0; --chunk) {
-        const int d = chunk * 32 + (31 - tid);  // lane 0 holds the highest digit of the chunk
-        const unsigned c = hist[d];
-        unsigned incl = c;  // inclusive count over higher digits within the chunk
+    // thread j < 256 handles bin 255 - j: its inclusive prefix over j is the count of keys whose
+    // digit is >= that bin
+    unsigned c = 0u, incl = 0u;
+    if (tid < 256) {
+      c = hist[255 - tid];
+      incl = c;
 #pragma unroll
-        for (int off = 1; off < 32; off <<= 1) {
-          const unsigned o = __shfl_up_sync(0xffffffffu, incl, off);
-          if (tid >= off) incl += o;
-        }
-        const bool hit = cum + incl >= remaining && cum + incl - c < remaining;
-        const unsigned b = __ballot_sync(0xffffffffu, hit);
-        if (b) {
-          const int src = __ffs(b) - 1;
-          const unsigned above = __shfl_sync(0xffffffffu, cum + incl - c, src);
-          found = chunk * 32 + (31 - src);
-          rem_out = remaining - above;
-        }
-        cum += __shfl_sync(0xffffffffu, incl, 31);
+      for (int off = 1; off < 32; off <<= 1) {
+        const unsigned o = __shfl_up_sync(0xffffffffu, incl, off);
+        if (lane >= off) incl += o;
       }
-      if (tid == 0) {
-        s_digit = (unsigned)found;
-        s_rem = rem_out;
+      if (lane == 31) s_scan[warp] = incl;
+    }
+    __syncthreads();
+    if (tid < 256) {
+      for (int w = 0; w < warp; ++w) incl += s_scan[w];
+      const unsigned above = incl - c;
+      if (above < remaining && incl >= remaining) {
+        s_digit = 255u - (unsigned)tid;
+        s_rem = remaining - above;
       }
     }
     __syncthreads();
@@ -141,30 +145,36 @@ __device__ void select_topk(const float* dev, int n, int budget, const int64_t* 
     remaining = s_rem;
     __syncthreads();
   }
-  // prefix is the key of the budget-th largest value; `remaining` of its ties are taken,
-  // lowest indices first.
-  unsigned eq_base = 0u, sel_base = 0u;
-#pragma unroll 1
-  for (int base = 0; base < n; base += kThreads) {
-    const int i = base + tid;
-    const unsigned key = i < n ? order_key(__ldcg(dev + i)) : 0u;
-    const bool gt = i < n && key > prefix;
-    const bool eq = i < n && key == prefix;
-    unsigned teq, tsel;
-    const unsigned eq_rank = eq_base + block_scan(eq, s_warp, teq);
-    const bool sel = gt || (eq && eq_rank < remaining);
-    const unsigned r = sel_base + block_scan(sel, s_warp, tsel);
+  // prefix is the key of the budget-th largest value; `remaining` of its ties are taken, lowest
+  // indices first.
+  unsigned gt = 0u, eq = 0u;
+  for (int i = lo; i < hi; ++i) {
+    const unsigned key = order_key(__ldcg(dev + i));
+    gt += key > prefix;
+    eq += key == prefix;
+  }
+  unsigned tot;
+  const unsigned eq_before = block_exclusive_sum(eq, s_scan, tot);
+  const unsigned take_eq = eq_before >= remaining ? 0u : min(eq, remaining - eq_before);
+  unsigned r = block_exclusive_sum(gt + take_eq, s_scan, tot);
+  unsigned taken = 0u;
+  for (int i = lo; i < hi; ++i) {
+    const unsigned key = order_key(__ldcg(dev + i));
+    bool sel = key > prefix;
+    if (key == prefix && taken < take_eq) {
+      sel = true;
+      ++taken;
+    }
     if (sel) {
       sel_idx[r] = i;
       if (sel_pos) sel_pos[r] = cand_pos[i];
+      ++r;
     }
-    eq_base += teq;
-    sel_base += tsel;
   }
 }
 
 template <typename T, int E>
-__global__ void __launch_bounds__(kThreads)
+__global__ void __launch_bounds__(kThreads, 2)
     deviation_topk_kernel(const T* __restrict__ k1, const T* __restrict__ v1, long long f_st, long long f_sh,
                           const T* __restrict__ K1, const T* __restrict__ V1, long long c_st, long long c_sh,
                           long long T_cache, const int64_t* __restrict__ cand_pos, int n, int H, int budget,
@@ -180,17 +190,28 @@ __global__ void __launch_bounds__(kThreads)
       dev = __int_as_float(0x7fc00000);
     } else {
       float a = 0.f, b = 0.f;
+      constexpr int HU = E <= 4 ? 2 : 1;  // heads whose rows are in flight together
 #pragma unroll 1
-      for (int h = 0; h < H; ++h) {
-        float fk[E], ck[E], fv[E], cv[E];
-        const long long fo = (long long)t * f_st + (long long)h * f_sh + lane * E;
-        const long long co = pos * c_st + (long long)h * c_sh + lane * E;
-        load_row<T, E>(k1 + fo, fk);
-        load_row<T, E>(K1 + co, ck);
-        load_row<T, E>(v1 + fo, fv);
-        load_row<T, E>(V1 + co, cv);
-        a = __fadd_rn(a, row_norm<E>(fk, ck));
-        b = __fadd_rn(b, row_norm<E>(fv, cv));
+      for (int h0 = 0; h0 < H; h0 += HU) {
+        float fk[HU][E], ck[HU][E], fv[HU][E], cv[HU][E];
+#pragma unroll
+        for (int j = 0; j < HU; ++j) {
+          if (h0 + j < H) {
+            const long long fo = (long long)t * f_st + (long long)(h0 + j) * f_sh + lane * E;
+            const long long co = pos * c_st + (long long)(h0 + j) * c_sh + lane * E;
+            load_row<T, E>(k1 + fo, fk[j]);
+            load_row<T, E>(K1 + co, ck[j]);
+            load_row<T, E>(v1 + fo, fv[j]);
+            load_row<T, E>(V1 + co, cv[j]);
+          }
+        }
+#pragma unroll
+        for (int j = 0; j < HU; ++j) {
+          if (h0 + j < H) {
+            a = __fadd_rn(a, row_norm<E>(fk[j], ck[j]));
+            b = __fadd_rn(b, row_norm<E>(fv[j], cv[j]));
+          }
+        }
       }
       dev = __fadd_rn(a, b);
     }

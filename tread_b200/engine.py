@@ -1,0 +1,226 @@
+"""Reuse engine: build a request's KV cache from content-addressed chunk blocks, on B200.
+
+Same contract as tread/engine.py: a request is [prefix][doc_1]...[doc_N][query] given as
+separate segments; the prefix is reused as an exact prefix, each doc block is computed once
+after the prefix (base position P), cached under a key chained from the prefix key, and
+re-rotated to wherever it lands in later requests; optional selective recompute repairs the
+missing cross-doc attention. Hit/miss accounting and store decisions match the reference.
+
+B200 changes inside `prefill`:
+  - assembly is ONE launch of tread_rope_gather_append over all hit blocks straight into the
+    request cache [L, 1, Hkv, T + q, D] (reference: one rotate per block + torch.cat); blocks
+    fetched from the pinned-host tier are assembled by a second launch that waits only on their
+    transfer events, so those copies overlap the first launch;
+  - the query segment's rows ride along in the recompute pass (same layer launches, one weight
+    read per layer), and with ratio 0 they are the only rows: every row attends to the keys at
+    positions <= its own, which reproduces blend-then-query exactly;
+  - stage timers keep the reference's names: `blend` covers the layer pass (recompute rows and
+    query rows), `query` the final norm + lm_head and the cache handle.
+"""
+import time
+from dataclasses import dataclass, field
+
+import torch
+
+from tread_b200 import kernels
+from tread_b200.blend import rows_of, select, to_cache
+from tread_b200.graphs import SubsetRunner
+from tread_b200.store import BlockStore, block_key
+
+
+@dataclass
+class RequestStats:
+    hits: int = 0
+    misses: int = 0
+    tokens_reused: int = 0
+    tokens_prefilled: int = 0
+    recompute_eff: float = 0.0
+    t: dict = field(default_factory=dict)  # stage -> seconds
+
+
+class _Tmp:
+    """Uncached block (store budget too small for it): same fields as store.Block."""
+
+    def __init__(self, K, V, base):
+        self.K, self.V, self.base, self.n_tokens = K, V, base, K.shape[-2]
+        self.ready = None
+
+    def wait(self, stream=None):
+        pass
+
+
+class Engine:
+    def __init__(self, model, store: BlockStore, graphs=False):
+        self.model = model
+        self.store = store
+        self.runner = SubsetRunner(model) if graphs else None
+        cfg = model.config
+        self.sig = (cfg._name_or_path, str(model.dtype), getattr(cfg, "rope_theta", None),
+                    getattr(cfg, "rope_scaling", None))
+        self.net = rows_of(model)
+
+    def _sync(self):
+        if torch.cuda.is_available():
+            torch.cuda.synchronize()
+
+    # -- blocks ----------------------------------------------------------------------------------
+    def _prefill_rows(self, ids, base_cache=None, P=0):
+        """K/V [L, 1, Hkv, P + n, D] of `ids` run at positions P.. after an existing prefix cache."""
+        net = self.net
+        n = len(ids)
+        K, V = net.new_cache(P + n)
+        if base_cache is not None and P:
+            kernels.rope_gather_append([(base_cache[0], base_cache[1], 0, 0)], K, V, net.inv_freq, net.attn_scaling)
+        pos = torch.arange(P, P + n, device=ids.device)
+        net.run(net.embed_ids(ids), pos, list(K.unbind(0)), list(V.unbind(0)))
+        return K, V
+
+    @torch.inference_mode()
+    def prefix_block(self, prefix_ids, st, namespace=""):
+        # Doc keys derive from this key, so a namespace isolates a tenant's whole block tree.
+        key = block_key(*self.sig, namespace, "prefix", prefix_ids)
+        b = self.store.get(key, wait=False)
+        if b is None:
+            st.misses += 1
+            st.tokens_prefilled += len(prefix_ids)
+            K, V = self._prefill_rows(prefix_ids)
+            b = self.store.put(key, K, V, 0) or _Tmp(K, V, 0)
+        else:
+            st.hits += 1
+            st.tokens_reused += len(prefix_ids)
+        return key, b
+
+    @torch.inference_mode()
+    def doc_blocks(self, prefix_key, pb, docs, st):
+        """Look up every doc's block; prefill the misses after the cached prefix (tread/engine.py:59-96).
+
+        Each missed doc runs at positions P.. over [prefix KV | its own KV], so it sees the prefix
+        and itself, never another doc: the reference's block-diagonal packed prefill, per doc.
+        """
+        keys = [block_key(*self.sig, prefix_key, d) for d in docs]
+        blocks = [self.store.get(k, wait=False) for k in keys]
+        miss = [i for i, b in enumerate(blocks) if b is None]
+        st.hits += len(docs) - len(miss)
+        st.tokens_reused += sum(len(d) for d, b in zip(docs, blocks) if b is not None)
+        if not miss:
+            return blocks
+        st.misses += len(miss)
+        P = pb.n_tokens
+        pb.wait()
+        for i in miss:
+            st.tokens_prefilled += len(docs[i])
+            Kf, Vf = self._prefill_rows(docs[i], (pb.K, pb.V), P)
+            K, V = Kf[..., P:, :].contiguous(), Vf[..., P:, :].contiguous()
+            blocks[i] = self.store.put(keys[i], K, V, P) or _Tmp(K, V, P)
+        return blocks
+
+    # -- request -----------------------------------------------------------------------------------
+    @torch.inference_mode()
+    def prefill(self, prefix_ids, docs, query_ids, ratio=0.0, policy="deviation", namespace=""):
+        """Build the context cache from blocks, optionally blend, run the query.
+
+        Returns (logits of the last query position, DynamicCache for decoding, RequestStats).
+        """
+        net = self.net
+        st = RequestStats()
+        self._sync()
+        t0 = time.perf_counter()
+
+        pkey, pb = self.prefix_block(prefix_ids, st, namespace)
+        blocks = self.doc_blocks(pkey, pb, docs, st)
+        P = pb.n_tokens
+        nq = len(query_ids)
+        T = P + sum(len(d) for d in docs)
+        K, V = self._request_cache(T + nq)
+        segs, pending, cands = [(pb, 0, 0)], [], []
+        offset = P
+        for d, b in zip(docs, blocks):
+            segs.append((b, offset - b.base, offset))
+            cands.append(torch.arange(offset, offset + len(d), device=d.device))
+            offset += len(d)
+        ready = [s for s in segs if s[0].ready is None or s[0].ready.query()]
+        pending = [s for s in segs if not (s[0].ready is None or s[0].ready.query())]
+        for group in (ready, pending):
+            if group:
+                for b, _, _ in group:
+                    b.wait()
+                kernels.rope_gather_append([(b.K, b.V, dl, o) for b, dl, o in group], K, V, net.inv_freq,
+                                           net.attn_scaling)
+        Kl, Vl = list(K.unbind(0)), list(V.unbind(0))
+        self._sync()
+        t1 = time.perf_counter()
+
+        hq = net.embed_ids(query_ids)
+        qpos = torch.arange(T, T + nq, device=query_ids.device)
+        start, rows_h, rows_pos = 0, hq, qpos
+        if ratio > 0 and cands:
+            ctx = torch.cat([prefix_ids] + list(docs))
+            S, hS, start, all_c, hx = select(self.model, ctx, Kl, Vl, cands, ratio, policy, inplace=True,
+                                             extra=(hq, qpos))
+            if len(S):
+                if hS is None:
+                    hS = net.embed_ids(ctx[S])
+                if hx is not None:
+                    hq = hx  # query rows already went through layer 0 with the candidates
+                rows_h, rows_pos = torch.cat([hS, hq]), torch.cat([S, qpos])
+                n, L = len(all_c), net.L
+                st.recompute_eff = (len(S) * (L - start) + start * n) / (n * L)
+            else:
+                start = 0
+        if self.runner is not None and self.runner.worth_it(T + nq):
+            h = self.runner.run_rows(rows_h, rows_pos, Kl, Vl, start)
+        else:
+            h = net.run(rows_h, rows_pos, Kl, Vl, start)
+        self._sync()
+        t2 = time.perf_counter()
+
+        logits = net.logits(h[-1:])[0]
+        cache = to_cache(Kl, Vl)
+        self._sync()
+        t3 = time.perf_counter()
+        st.t = dict(assemble=t1 - t0, blend=t2 - t1, query=t3 - t2, ttft=t3 - t0)
+        return logits, cache, st
+
+    def _request_cache(self, T):
+        shape = (self.net.L, 1, self.net.Hkv, T, self.net.D)
+        return (torch.empty(shape, dtype=self.net.dtype, device=self.net.device),
+                torch.empty(shape, dtype=self.net.dtype, device=self.net.device))
+
+    @torch.inference_mode()
+    def prefill_prefix_only(self, prefix_ids, docs, query_ids):
+        """Baseline: exact-prefix caching only (tread/engine.py:138-152). The prefix comes from the
+        store; every doc is prefilled again."""
+        st = RequestStats()
+        self._sync()
+        t0 = time.perf_counter()
+        _, pb = self.prefix_block(prefix_ids, st)
+        pb.wait()
+        rest = torch.cat(list(docs) + [query_ids])
+        st.tokens_prefilled += len(rest) - len(query_ids)
+        P = pb.n_tokens
+        K, V = self.net.new_cache(P + len(rest))
+        kernels.rope_gather_append([(pb.K, pb.V, 0, 0)], K, V, self.net.inv_freq, self.net.attn_scaling)
+        Kl, Vl = list(K.unbind(0)), list(V.unbind(0))
+        h = self.net.run(self.net.embed_ids(rest), torch.arange(P, P + len(rest), device=rest.device), Kl, Vl)
+        logits = self.net.logits(h[-1:])[0]
+        self._sync()
+        st.t = dict(ttft=time.perf_counter() - t0)
+        return logits, to_cache(Kl, Vl), st
+
+
+@torch.inference_mode()
+def prefill_full(model, prefix_ids, docs, query_ids):
+    """Baseline: no caching at all (tread/engine.py:155-166), on the same layer math."""
+    net = rows_of(model)
+    if torch.cuda.is_available():
+        torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    ids = torch.cat([prefix_ids] + list(docs) + [query_ids])
+    K, V = net.new_cache(len(ids))
+    Kl, Vl = list(K.unbind(0)), list(V.unbind(0))
+    h = net.run(net.embed_ids(ids), torch.arange(len(ids), device=ids.device), Kl, Vl)
+    logits = net.logits(h[-1:])[0]
+    if torch.cuda.is_available():
+        torch.cuda.synchronize()
+    st = RequestStats(tokens_prefilled=len(ids) - len(query_ids), t=dict(ttft=time.perf_counter() - t0))
+    return logits, to_cache(Kl, Vl), st

@@ -206,3 +206,70 @@ def deviation_topk(k1, v1, K1, V1, cand_pos, budget, dev_out=None, sel_idx=None,
             _stream_arg(stream, dev))
     C.check(rc, "tread_deviation_topk")
     return dev_out, sel_idx, sel_pos
+
+
+# ---- recompute rows: RoPE + K/V splice, attention -------------------------------------------
+
+def _layer_cache(K, name):
+    """A layer cache view [Hkv, T, D] (or [1, Hkv, T, D]) with contiguous [T, D] per head."""
+    C.require_cuda(K, name)
+    if K.dim() == 4:
+        K = K[0]
+    if K.dim() != 3 or K.stride(2) != 1 or K.stride(1) != K.shape[2]:
+        raise ValueError(f"{name} must be [Hkv, T, D] with contiguous [T, D] planes")
+    return K
+
+
+def rope_rows(qkv, pos, Hq, Hkv, D, q_out, K, V, inv_freq, attn_scaling=1.0, err=None, stream=None,
+              kv_by_row=False):
+    """Rotate the rows' q heads into q_out [R, Hq, D] (skipped if q_out is None) and splice their
+    rotated k / plain v into the layer cache K/V at `pos` (tread/blend.py:82-90,106); with
+    kv_by_row, row r's k/v go to cache row r instead (dense [Hkv, R, D] outputs).
+    qkv: [R, >= (Hq+2Hkv)*D] with unit column stride."""
+    C.require_cuda(qkv, "qkv")
+    K = _layer_cache(K, "K")
+    V = _layer_cache(V, "V")
+    R = qkv.shape[0]
+    if qkv.dim() != 2 or qkv.stride(1) != 1:
+        raise ValueError("qkv must be 2-D with unit column stride")
+    if pos.dtype != torch.int64 or pos.numel() != R or not pos.is_contiguous():
+        raise ValueError("pos must be a contiguous int64 tensor of length R")
+    if q_out is not None and (q_out.shape != (R, Hq, D) or not q_out.is_contiguous() or q_out.dtype != qkv.dtype):
+        raise ValueError("q_out must be a contiguous [R, Hq, D] tensor of qkv's dtype")
+    if not (qkv.dtype == K.dtype == V.dtype) or K.stride(0) != V.stride(0) or K.shape != V.shape:
+        raise ValueError("dtype/stride mismatch between qkv and the cache")
+    if K.shape[0] != Hkv or K.shape[2] != D:
+        raise ValueError("cache head count / head_dim do not match")
+    inv = inv_freq.tolist() if isinstance(inv_freq, torch.Tensor) else list(inv_freq)
+    with torch.cuda.device(qkv.device):
+        rc = C.lib().tread_rope_rows(qkv.data_ptr(), qkv.stride(0), pos.data_ptr(), R, Hq, Hkv, D,
+                                     None if q_out is None else q_out.data_ptr(), K.data_ptr(), V.data_ptr(),
+                                     K.stride(0), K.shape[1], int(bool(kv_by_row)), C.f32_array(inv),
+                                     float(attn_scaling), C.dtype_code(qkv.dtype),
+                                     None if err is None else err.data_ptr(), _stream_arg(stream, qkv.device))
+    C.check(rc, "tread_rope_rows")
+    return q_out
+
+
+def attn_rows(q, K, V, pos, out=None, sm_scale=None, err=None, stream=None):
+    """Each row of q [R, Hq, D] attends to keys at positions <= pos[row] of the layer cache K/V
+    ([Hkv, T, D]) with GQA (tread/blend.py:76,110). Returns out [R, Hq, D]."""
+    C.require_cuda(q, "q")
+    K = _layer_cache(K, "K")
+    V = _layer_cache(V, "V")
+    R, Hq, D = q.shape
+    Hkv = K.shape[0]
+    if not q.is_contiguous() or K.shape != V.shape or K.stride(0) != V.stride(0) or K.shape[2] != D:
+        raise ValueError("q must be contiguous [R, Hq, D]; K/V [Hkv, T, D] with equal strides")
+    if pos.dtype != torch.int64 or pos.numel() != R or not pos.is_contiguous():
+        raise ValueError("pos must be a contiguous int64 tensor of length R")
+    if out is None:
+        out = torch.empty_like(q)
+    if sm_scale is None:
+        sm_scale = D ** -0.5
+    with torch.cuda.device(q.device):
+        rc = C.lib().tread_attn_rows(q.data_ptr(), K.data_ptr(), V.data_ptr(), K.stride(0), K.shape[1], pos.data_ptr(),
+                                     R, Hq, Hkv, D, float(sm_scale), out.data_ptr(), C.dtype_code(q.dtype),
+                                     None if err is None else err.data_ptr(), _stream_arg(stream, q.device))
+    C.check(rc, "tread_attn_rows")
+    return out

@@ -1,0 +1,119 @@
+"""Qwen2 decoder math over token rows at arbitrary positions, on tread_b200 kernels.
+
+The reference drives HF's Qwen2 modules directly (tread/blend.py:82-114, tread/engine.py:86-88,
+131-132). This module owns the same layer arithmetic (weights taken from the HF module) so
+that every path the hot path needs is one primitive: a set of token rows, each at its own
+absolute position, runs through layers [l0, l1) against per-layer KV caches, with
+
+    x = RMSNorm(h);  qkv = x @ Wqkv^T + b            (one GEMM, cuBLAS)
+    RoPE(q, k at pos) ; K[pos], V[pos] = k, v        (tread_rope_rows)
+    o = attention(q, K, V, key_pos <= pos)           (tread_attn_rows)
+    h = h + o @ Wo^T ; h = h + down(silu(gate) * up) (GEMMs; SwiGLU)
+
+Rows are: recomputed tokens (blend), the query segment, a prefix or a doc being prefilled.
+A row only ever sees keys at positions <= its own, which is the causal mask of a prefill, the
+subset mask of tread/blend.py:76, and the query's causal attention over the assembled cache.
+"""
+import torch
+import torch.nn.functional as F
+
+from tread_b200 import kernels
+
+
+class Qwen2Rows:
+    def __init__(self, model):
+        cfg = model.config
+        self.model = model
+        self.L = cfg.num_hidden_layers
+        self.hidden = cfg.hidden_size
+        self.Hq = cfg.num_attention_heads
+        self.Hkv = cfg.num_key_value_heads
+        self.D = getattr(cfg, "head_dim", None) or cfg.hidden_size // cfg.num_attention_heads
+        self.eps = cfg.rms_norm_eps
+        self.dtype = model.dtype
+        self.device = model.device
+        rot = model.model.rotary_emb
+        self.inv_freq = rot.inv_freq.float().cpu().tolist()
+        self.attn_scaling = float(getattr(rot, "attention_scaling", 1.0))
+        if getattr(rot, "rope_type", "default") not in ("default", "linear", "llama3"):
+            # position-dependent frequency schemes (dynamic NTK) would need a per-request inv_freq
+            raise NotImplementedError(f"rope_type {rot.rope_type} is not supported")
+        self.embed = model.model.embed_tokens.weight
+        self.norm_w = model.model.norm.weight
+        self.lm_head = model.lm_head.weight
+        self.layers = []
+        with torch.no_grad():
+            for layer in model.model.layers:
+                a, m = layer.self_attn, layer.mlp
+                self.layers.append(dict(
+                    ln1=layer.input_layernorm.weight,
+                    ln1_eps=layer.input_layernorm.variance_epsilon,
+                    wqkv=torch.cat([a.q_proj.weight, a.k_proj.weight, a.v_proj.weight], 0).contiguous(),
+                    bqkv=torch.cat([a.q_proj.bias, a.k_proj.bias, a.v_proj.bias], 0).contiguous(),
+                    wo=a.o_proj.weight,
+                    ln2=layer.post_attention_layernorm.weight,
+                    ln2_eps=layer.post_attention_layernorm.variance_epsilon,
+                    wgu=torch.cat([m.gate_proj.weight, m.up_proj.weight], 0).contiguous(),
+                    wd=m.down_proj.weight,
+                    inter=m.gate_proj.weight.shape[0],
+                ))
+        self.err = torch.zeros(4, dtype=torch.int32, device=self.device)
+
+    # -- elementwise pieces (HF Qwen2RMSNorm / SwiGLU semantics) --------------------------------
+    @staticmethod
+    def rmsnorm(x, w, eps):
+        x32 = x.float()
+        var = x32.pow(2).mean(-1, keepdim=True)
+        return w * (x32 * torch.rsqrt(var + eps)).to(x.dtype)
+
+    def embed_ids(self, ids):
+        return F.embedding(ids, self.embed)
+
+    # -- one layer over rows ----------------------------------------------------------------------
+    def qkv(self, l, h):
+        p = self.layers[l]
+        return torch.addmm(p["bqkv"], self.rmsnorm(h, p["ln1"], p["ln1_eps"]), p["wqkv"].t())
+
+    def layer(self, l, h, pos, K, V, qkv=None):
+        """h: [R, hidden] rows at positions pos (int64 [R]); K, V: layer-l caches [1, Hkv, T, D]
+        (or [Hkv, T, D]); the rows' k/v are written into them. Returns the new h."""
+        p = self.layers[l]
+        R = h.shape[0]
+        if qkv is None:
+            qkv = self.qkv(l, h)
+        q = torch.empty(R, self.Hq, self.D, dtype=h.dtype, device=h.device)
+        kernels.rope_rows(qkv, pos, self.Hq, self.Hkv, self.D, q, K, V, self.inv_freq, self.attn_scaling, self.err)
+        o = kernels.attn_rows(q, K, V, pos, err=self.err)
+        h = torch.addmm(h, o.view(R, -1), p["wo"].t())
+        x = self.rmsnorm(h, p["ln2"], p["ln2_eps"])
+        gu = x @ p["wgu"].t()
+        a = F.silu(gu[:, :p["inter"]]) * gu[:, p["inter"]:]
+        return torch.addmm(h, a, p["wd"].t())
+
+    def layer1_kv(self, h):
+        """Layer-1 k (un-rotated k is never needed: rotated at the row position like the cache) and
+        v of rows h (layer-0 outputs): returns the packed qkv projection of layer 1."""
+        return self.qkv(1, h)
+
+    def run(self, h, pos, Ks, Vs, l0=0, l1=None):
+        for l in range(l0, self.L if l1 is None else l1):
+            h = self.layer(l, h, pos, Ks[l], Vs[l])
+        return h
+
+    def logits(self, h_last):
+        """Final RMSNorm + lm_head of the given rows (HF Qwen2Model.norm, Qwen2ForCausalLM.lm_head)."""
+        x = self.rmsnorm(h_last, self.norm_w, self.model.model.norm.variance_epsilon)
+        return x @ self.lm_head.t()
+
+    def new_cache(self, T):
+        """Zeroed per-request KV cache [L, 1, Hkv, T, D] for K and for V."""
+        shape = (self.L, 1, self.Hkv, T, self.D)
+        return (torch.zeros(shape, dtype=self.dtype, device=self.device),
+                torch.zeros(shape, dtype=self.dtype, device=self.device))
+
+    def check_errors(self):
+        """Raise if a kernel flagged an out-of-range row position (costs a device sync)."""
+        e = int(self.err.max().item())
+        if e:
+            self.err.zero_()
+            raise RuntimeError(f"tread_b200 kernel reported an out-of-range position (flags {e:#x})")
