@@ -105,6 +105,29 @@ int tread_deviation_topk(const void* k1, const void* v1, int64_t fresh_stride_to
                          tread_stream_t stream);
 
 /*
+ * Allocation-free variant of tread_deviation_topk. It has no counterpart in the reference; it
+ * exists for callers that cannot provide device scratch: serving loops whose device memory is
+ * owned by a pooling allocator reserved at start-up, loops that avoid cudaMalloc because it can
+ * synchronise the device, and FFI hosts with no device allocator. The selector's scratch (ticket
+ * and error words plus the fp32 deviation of every candidate) lives in a file-scope device array
+ * of 256 B + 4 B x TREAD_NOALLOC_MAX_CANDIDATES (about 256 KB) that every GPU loading the
+ * library holds until exit; the caller passes the same inputs and the sel_idx / sel_pos outputs
+ * as for tread_deviation_topk (the deviation values themselves are not returned).
+ *   - n > TREAD_NOALLOC_MAX_CANDIDATES is rejected with TREAD_ERR_INVALID;
+ *   - the first call on a device looks up the array's device address (cudaGetSymbolAddress with
+ *     that device current), so make that first call before any stream capture;
+ *   - every call clears the ticket words on `stream` and then reuses the shared array, so calls
+ *     that overlap on the GPU (different streams, or different host threads) race: order them;
+ *   - it calls no cudaMalloc / cudaFree.
+ */
+#define TREAD_NOALLOC_MAX_CANDIDATES 65536
+int tread_deviation_topk_noalloc(const void* k1, const void* v1, int64_t fresh_stride_tok,
+                                 int64_t fresh_stride_head, const void* K1, const void* V1,
+                                 int64_t cache_stride_tok, int64_t cache_stride_head, int64_t T_cache,
+                                 const int64_t* cand_pos, int n, int Hkv, int D, int budget, int dtype,
+                                 int64_t* sel_idx, int64_t* sel_pos, tread_stream_t stream);
+
+/*
  * RoPE at each row's absolute position + splice of the row's K/V into the layer cache.
  *
  * Replaces, per recomputed layer, tread/blend.py:82-90 (`_qkv`: q/k/v views of the

@@ -36,6 +36,11 @@ SIGNATURES = {
         [P, P, I64, I64, P, P, I64, I64, I64, P, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int,
          ctypes.c_int, P, P, P, P, P],
     ),
+    "tread_deviation_topk_noalloc": (
+        ctypes.c_int,
+        [P, P, I64, I64, P, P, I64, I64, I64, P, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int,
+         ctypes.c_int, P, P, P],
+    ),
     "tread_rope_rows": (
         ctypes.c_int,
         [P, I64, P, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int, P, P, P, I64, I64, ctypes.c_int, PF32,

@@ -303,3 +303,73 @@ extern "C" int tread_deviation_topk(const void* k1, const void* v1, int64_t fres
                                st);
   }
 }
+
+// ---- allocation-free variant -------------------------------------------------------------------
+//
+// Some callers cannot hand this library device scratch: serving loops whose HBM is owned
+// entirely by a pooling allocator reserved at start-up (a raw cudaMalloc there fails or
+// fragments memory outside the pool), latency-critical loops that avoid cudaMalloc because it
+// can synchronise the device, and thin FFI hosts (ctypes, cgo, JNI) that have no device
+// allocator of their own. For them the selector's scratch — the CTA ticket / error words and the
+// fp32 deviation of every candidate — lives in one file-scope device array instead, so the call
+// allocates nothing; the caller still passes every input and output.
+
+#include <mutex>
+
+namespace tread {
+namespace {
+
+constexpr int kNoAllocMaxCandidates = 65536;
+constexpr size_t kNoAllocTicketBytes = 256;
+// 256 B of ticket/flag words + 256 KB of per-candidate deviation; every GPU that loads the
+// library holds this array until the process exits.
+static __device__ __align__(256) unsigned char
+    g_selector_scratch[kNoAllocTicketBytes + sizeof(float) * kNoAllocMaxCandidates];
+
+constexpr int kMaxDevices = 128;
+std::mutex g_scratch_mu;
+void* g_scratch_addr[kMaxDevices] = {};  // device address of g_selector_scratch, per device
+
+// Device address of the static scratch on the current device, looked up once per device.
+int scratch_address(void** out) {
+  int dev = -1;
+  TREAD_CHECK_CUDA(cudaGetDevice(&dev));
+  TREAD_CHECK_ARG(dev >= 0 && dev < kMaxDevices, "deviation_topk_noalloc: device %d out of range", dev);
+  std::lock_guard<std::mutex> lock(g_scratch_mu);
+  if (g_scratch_addr[dev] == nullptr) {
+    void* p = nullptr;
+    const cudaError_t e = cudaGetSymbolAddress(&p, g_selector_scratch);
+    if (e != cudaSuccess || p == nullptr) {
+      set_error("deviation_topk_noalloc: cudaGetSymbolAddress failed on device %d: %s", dev,
+                cudaGetErrorString(e));
+      return TREAD_ERR_CUDA;
+    }
+    g_scratch_addr[dev] = p;
+  }
+  *out = g_scratch_addr[dev];
+  return TREAD_OK;
+}
+
+}  // namespace
+}  // namespace tread
+
+extern "C" int tread_deviation_topk_noalloc(const void* k1, const void* v1, int64_t fresh_stride_tok,
+                                            int64_t fresh_stride_head, const void* K1, const void* V1,
+                                            int64_t cache_stride_tok, int64_t cache_stride_head, int64_t T_cache,
+                                            const int64_t* cand_pos, int n, int Hkv, int D, int budget, int dtype,
+                                            int64_t* sel_idx, int64_t* sel_pos, tread_stream_t stream) {
+  using namespace tread;
+  TREAD_CHECK_ARG(n >= 0 && n <= kNoAllocMaxCandidates,
+                  "deviation_topk_noalloc: n=%d candidates exceeds the static scratch maximum of %d", n,
+                  kNoAllocMaxCandidates);
+  if (n == 0) return TREAD_OK;
+  void* scratch = nullptr;
+  const int rc = scratch_address(&scratch);
+  if (rc != TREAD_OK) return rc;
+  // The array keeps the previous call's contents: the ticket and error words must start at zero.
+  TREAD_CHECK_CUDA(cudaMemsetAsync(scratch, 0, kNoAllocTicketBytes, reinterpret_cast<cudaStream_t>(stream)));
+  float* dev = reinterpret_cast<float*>(static_cast<unsigned char*>(scratch) + kNoAllocTicketBytes);
+  return tread_deviation_topk(k1, v1, fresh_stride_tok, fresh_stride_head, K1, V1, cache_stride_tok,
+                              cache_stride_head, T_cache, cand_pos, n, Hkv, D, budget, dtype, dev, sel_idx, sel_pos,
+                              scratch, stream);
+}
