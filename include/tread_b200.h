@@ -158,10 +158,14 @@ int tread_rope_rows(const void* qkv, int64_t ld_qkv, const int64_t* pos, int R, 
  * (tread/engine.py:131-132). q, out: [R, Hq, D]; K/V: one layer's [Hkv, T_cache, D] at head
  * stride cache_stride_head; softmax in fp32 with scores scaled by sm_scale. Positions outside
  * [0, T_cache) skip their row and set bit 1 of *err_flag (may be NULL).
+ * bf16 / fp16 with D == 128 run on the tcgen05 tensor-core kernel (TMA-fed, S and O in TMEM);
+ * a bounded mbarrier wait that gives up sets bit 2 of *err_flag. flags bit 0 forces the
+ * CUDA-core kernel (used for fp32 and the other head dims).
  */
+#define TREAD_ATTN_FORCE_CUDA_CORES 1
 int tread_attn_rows(const void* q, const void* K_cache, const void* V_cache, int64_t cache_stride_head,
                     int64_t T_cache, const int64_t* q_pos, int R, int Hq, int Hkv, int D, float sm_scale,
-                    void* out, int dtype, void* err_flag, tread_stream_t stream);
+                    void* out, int dtype, int flags, void* err_flag, tread_stream_t stream);
 
 /*
  * Block-store tier transfers (pinned host <-> HBM), stream-ordered DMA copies.

@@ -286,3 +286,39 @@ def test_bf16_engine_runs_close_to_full_prefill(cuda):
     ref, _, _ = prefill_full(model, prefix, order, query)
     out, _, st = eng.prefill(prefix, order, query, ratio=1.0, policy="boundary")
     assert st.misses == 0 and kl(ref, out) < 1e-3
+
+
+def _sdpa_ref(q, K, V, pos):
+    """fp32 torch reference of tread/blend.py:76,110: [R, Hq, D] rows against [Hkv, T, D]."""
+    R, Hq, D = q.shape
+    Hkv, T, _ = K.shape
+    G = Hq // Hkv
+    qf = q.float().transpose(0, 1)  # [Hq, R, D]
+    Kf = K.float().repeat_interleave(G, 0)
+    Vf = V.float().repeat_interleave(G, 0)
+    mask = torch.arange(T, device=q.device)[None, :] <= pos[:, None]
+    o = F.scaled_dot_product_attention(qf[None], Kf[None], Vf[None], attn_mask=mask[None, None])[0]
+    return o.transpose(0, 1)
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+@pytest.mark.parametrize("R,Hq,Hkv,T", [(17, 7, 1, 150), (300, 14, 2, 1000), (1651, 28, 4, 8256), (129, 8, 8, 129)])
+def test_tensor_core_attention_matches_fp32_reference(cuda, dtype, R, Hq, Hkv, T):
+    gen = torch.Generator(device=cuda).manual_seed(R + T)
+    D = 128
+    q = torch.randn(R, Hq, D, device=cuda, generator=gen).to(dtype)
+    K = torch.randn(Hkv, T, D, device=cuda, generator=gen).to(dtype)
+    V = torch.randn(Hkv, T, D, device=cuda, generator=gen).to(dtype)
+    pos = torch.sort(torch.randperm(T, device=cuda, generator=gen)[:R]).values
+    if R > 64:
+        pos[-16:] = torch.arange(T - 16, T, device=cuda)  # query rows at the end of the cache
+    err = torch.zeros(4, dtype=torch.int32, device=cuda)
+    o = kernels.attn_rows(q, K, V, pos, err=err)
+    o_cc = kernels.attn_rows(q, K, V, pos, err=err, cuda_cores=True)
+    torch.cuda.synchronize()
+    assert err.max().item() == 0
+    idx = torch.arange(0, R, max(1, R // 200), device=cuda)
+    ref = _sdpa_ref(q[idx], K, V, pos[idx])
+    tol = 2e-2 if dtype == torch.bfloat16 else 4e-3
+    torch.testing.assert_close(o[idx].float(), ref, rtol=0, atol=tol)
+    torch.testing.assert_close(o.float(), o_cc.float(), rtol=0, atol=tol)

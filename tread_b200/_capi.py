@@ -48,7 +48,8 @@ SIGNATURES = {
     ),
     "tread_attn_rows": (
         ctypes.c_int,
-        [P, P, P, I64, I64, P, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int, F32, P, ctypes.c_int, P, P],
+        [P, P, P, I64, I64, P, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int, F32, P, ctypes.c_int,
+         ctypes.c_int, P, P],
     ),
     "tread_kv_fetch": (ctypes.c_int, [P, P, ctypes.c_size_t, P]),
     "tread_kv_spill": (ctypes.c_int, [P, P, ctypes.c_size_t, P]),

@@ -7,8 +7,8 @@
 // head of the GQA group; the group's warps share each 32-key K/V tile staged in shared memory
 // (fp32), and every warp keeps a flash-style online softmax (running max / sum, fp32).
 //
-// This path serves fp32 / fp16 and any head_dim in {64, 128, 256}; bf16 with head_dim 128 is
-// dispatched to the tensor-core kernel when the library is built with it.
+// This path serves fp32 and head_dims 64 / 256 (and any dtype when the caller asks for it);
+// bf16 / fp16 with head_dim 128 run on the tensor-core kernel in attn_tc.cu.
 #include "common.cuh"
 
 namespace tread {
@@ -124,6 +124,10 @@ int dispatch_d(int D, const void* q, const void* K, const void* V, long long c_s
 
 }  // namespace
 
+int attn_rows_dispatch(const void* q, const void* K, const void* V, long long c_sh, long long T_cache,
+                       const int64_t* pos, int R, int Hq, int Hkv, int D, float sm_scale, void* out, int dtype,
+                       unsigned* err, cudaStream_t st, int force_simt);
+
 // CUDA-core recompute attention (all dtypes); the tensor-core path calls back into it for
 // shapes it does not cover.
 int attn_rows_simt(const void* q, const void* K, const void* V, long long c_sh, long long T_cache, const int64_t* pos,
@@ -141,7 +145,7 @@ int attn_rows_simt(const void* q, const void* K, const void* V, long long c_sh, 
 
 extern "C" int tread_attn_rows(const void* q, const void* K_cache, const void* V_cache, int64_t cache_stride_head,
                                int64_t T_cache, const int64_t* q_pos, int R, int Hq, int Hkv, int D, float sm_scale,
-                               void* out, int dtype, void* err_flag, tread_stream_t stream) {
+                               void* out, int dtype, int flags, void* err_flag, tread_stream_t stream) {
   using namespace tread;
   TREAD_CHECK_ARG(R >= 0, "attn_rows: R < 0");
   if (R == 0) return TREAD_OK;
@@ -152,6 +156,8 @@ extern "C" int tread_attn_rows(const void* q, const void* K_cache, const void* V
   TREAD_CHECK_ARG(T_cache > 0 && cache_stride_head >= T_cache * D, "attn_rows: bad cache geometry");
   TREAD_CHECK_ARG(R <= 2147483647 && Hkv <= 65535, "attn_rows: grid too large");
   TREAD_CHECK_ARG(dtype_size(dtype) != 0, "attn_rows: unknown dtype %d", dtype);
-  return attn_rows_simt(q, K_cache, V_cache, cache_stride_head, T_cache, q_pos, R, Hq, Hkv, D, sm_scale, out, dtype,
-                        static_cast<unsigned*>(err_flag), reinterpret_cast<cudaStream_t>(stream));
+  TREAD_CHECK_ARG((flags & ~1) == 0, "attn_rows: unknown flags %#x", flags);
+  return attn_rows_dispatch(q, K_cache, V_cache, cache_stride_head, T_cache, q_pos, R, Hq, Hkv, D, sm_scale, out,
+                            dtype, static_cast<unsigned*>(err_flag), reinterpret_cast<cudaStream_t>(stream),
+                            flags & 1);
 }

@@ -251,9 +251,10 @@ def rope_rows(qkv, pos, Hq, Hkv, D, q_out, K, V, inv_freq, attn_scaling=1.0, err
     return q_out
 
 
-def attn_rows(q, K, V, pos, out=None, sm_scale=None, err=None, stream=None):
+def attn_rows(q, K, V, pos, out=None, sm_scale=None, err=None, stream=None, cuda_cores=False):
     """Each row of q [R, Hq, D] attends to keys at positions <= pos[row] of the layer cache K/V
-    ([Hkv, T, D]) with GQA (tread/blend.py:76,110). Returns out [R, Hq, D]."""
+    ([Hkv, T, D]) with GQA (tread/blend.py:76,110). Returns out [R, Hq, D]. bf16/fp16 with D=128
+    run on tensor cores unless `cuda_cores`."""
     C.require_cuda(q, "q")
     K = _layer_cache(K, "K")
     V = _layer_cache(V, "V")
@@ -270,6 +271,7 @@ def attn_rows(q, K, V, pos, out=None, sm_scale=None, err=None, stream=None):
     with torch.cuda.device(q.device):
         rc = C.lib().tread_attn_rows(q.data_ptr(), K.data_ptr(), V.data_ptr(), K.stride(0), K.shape[1], pos.data_ptr(),
                                      R, Hq, Hkv, D, float(sm_scale), out.data_ptr(), C.dtype_code(q.dtype),
-                                     None if err is None else err.data_ptr(), _stream_arg(stream, q.device))
+                                     1 if cuda_cores else 0, None if err is None else err.data_ptr(),
+                                     _stream_arg(stream, q.device))
     C.check(rc, "tread_attn_rows")
     return out
