@@ -52,6 +52,8 @@ def parse():
     ap.add_argument("--seed", type=int, default=0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=10.0, help="CPU baseline sample budget")
+    ap.add_argument("--no-ttft", action="store_true", help="skip the configs[2] 7B TTFT leg")
+    ap.add_argument("--ttft-reps", type=int, default=5, help="timed warm requests per recompute ratio")
     return ap.parse_args()
 
 
@@ -293,6 +295,9 @@ def run_gpu(args):
 
     e2e = run_e2e(args, dev, pool_k, pool_v, ids, deltas, inv, world, rank) if args.e2e_steps > 0 else None
     selector = run_selector(args, dev, out_k, out_v, world)
+    del plans, pool_k, pool_v, out_k, out_v
+    torch.cuda.empty_cache()
+    ttft = None if args.no_ttft else run_ttft(args, dev, world)
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
@@ -316,6 +321,7 @@ def run_gpu(args):
             "cpu_baseline": cpu,
             "e2e": e2e,
             "selector": selector,
+            "ttft": ttft,
             "gpu_launches": args.steps,
             "clocks": clk,
         }
@@ -330,6 +336,114 @@ def run_gpu(args):
 # dram__bytes_read.sum + dram__bytes_write.sum of one launch of this kernel on this workload from an
 # ncu --set full capture (profiles/rope_gather_append_cfg2.md): 469.76 MB read + 421.91 MB written.
 TRAFFIC_PER_LAUNCH = 469762048 + 421905920
+
+
+def kl_div(a, b):
+    import torch.nn.functional as F
+
+    return F.kl_div(F.log_softmax(a.float(), -1), F.log_softmax(b.float(), -1), log_target=True,
+                    reduction="sum").item()
+
+
+def run_ttft(args, dev, world):
+    """random-init Qwen2.5-7B architecture (bf16), request = 256-token prefix +
+    16 docs x 496 + 64-token query (8256 tokens, seeded uniform ids). Pass 1 (cold) fills the block
+    store; every timed request is a fresh seeded permutation of the 16 docs (the reference's
+    reordered-RAG protocol, tread bench/bench_scaling.py:60-84). TTFT is end to end as a server sees
+    it: host token ids in (one H2D inside the call), first token out (D2H), p50 over --ttft-reps."""
+    import tread_b200.engine as te
+    from tread_b200 import BlockStore, Engine, prefill_full
+    from tread_b200.configs import random_model, random_tokens
+
+    t_init = time.perf_counter()
+    model = random_model("qwen2.5-7b", dtype=torch.bfloat16, device=dev, seed=args.seed, init_on_device=True)
+    V = model.config.vocab_size
+    g = torch.Generator().manual_seed(args.seed + 3)
+    prefix = random_tokens(256, V, g)
+    docs = [random_tokens(496, V, g) for _ in range(16)]
+    query = random_tokens(64, V, g)
+    eng = Engine(model, BlockStore(64 << 30))
+    init_s = time.perf_counter() - t_init
+    eng.prefill(prefix, docs, query)  # pass 1: cold, fills the store
+    pg = torch.Generator().manual_seed(args.seed + 5)
+    captured = {}
+    orig_select = te.select
+
+    def spy(*a, **kw):
+        res = orig_select(*a, **kw)
+        captured["S"] = res[0]
+        return res
+
+    out = {"workload": "configs[2] 7B reordered RAG, 256 + 16x496 + 64 tokens, bf16",
+           "init_s": round(init_s, 1), "ratios": {}}
+    for ratio in (0.0, 0.2, 0.5, 1.0):
+        times, stages = [], []
+        for rep in range(2 + args.ttft_reps):
+            order = [docs[i] for i in torch.randperm(16, generator=pg).tolist()]
+            te.select = spy
+            try:
+                torch.cuda.synchronize(dev)
+                t0 = time.perf_counter()
+                logits, cache, st = eng.prefill(prefix, order, query, ratio=ratio)
+                tok = int(logits.argmax().item())  # first token back on the host
+                t1 = time.perf_counter()
+            finally:
+                te.select = orig_select
+            del cache
+            if rep >= 2:
+                times.append(t1 - t0)
+                stages.append(st.t)
+        ref, _, _ = prefill_full(model, prefix, order, query)
+        r = {"p50_ms": round(statistics.median(times) * 1e3, 2), "min_ms": round(min(times) * 1e3, 2),
+             "stages_p50_ms": {k: round(statistics.median(s[k] for s in stages) * 1e3, 2) for k in stages[0]},
+             "kl_vs_full_prefill": round(kl_div(logits, ref), 5), "top1_eq_full": tok == int(ref.argmax()),
+             "recompute_eff": round(st.recompute_eff, 4)}
+        if ratio == 0.2 and "S" in captured:
+            r["attention"] = attention_roofline(eng, captured["S"], 16 * 496 + 256, 64, dev)
+        out["ratios"][str(ratio)] = r
+    full = []
+    for _ in range(3):  # no-reuse baseline on the same layer math
+        order = [docs[i] for i in torch.randperm(16, generator=pg).tolist()]
+        torch.cuda.synchronize(dev)
+        t0 = time.perf_counter()
+        logits, _, _ = prefill_full(model, prefix, order, query)
+        int(logits.argmax().item())
+        full.append(time.perf_counter() - t0)
+    out["full_prefill_p50_ms"] = round(statistics.median(full) * 1e3, 2)
+    del eng, model
+    torch.cuda.empty_cache()
+    return out
+
+
+def attention_roofline(eng, S, T_ctx, nq, dev):
+    """tread_attn_rows (tcgen05) on one layer of a 20% request: |S| recomputed rows + the query rows
+    against the 8256-token cache, timed alone with CUDA events. Algorithmic FLOPs per call =
+    4 * D * Hq * sum_rows(pos + 1) (QK^T and PV under the key_pos <= row_pos mask)."""
+    from tread_b200 import kernels
+
+    net = eng.net
+    pos = torch.cat([S.to(dev), torch.arange(T_ctx, T_ctx + nq, device=dev)])
+    R = len(pos)
+    gen = torch.Generator(device=dev).manual_seed(9)
+    q = torch.randn(R, net.Hq, net.D, device=dev, generator=gen).to(net.dtype)
+    K = torch.randn(net.Hkv, T_ctx + nq, net.D, device=dev, generator=gen).to(net.dtype)
+    Vc = torch.randn_like(K)
+    o = torch.empty_like(q)
+    for _ in range(3):
+        kernels.attn_rows(q, K, Vc, pos, out=o)
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(20)]
+    for a, b in ev:
+        a.record()
+        kernels.attn_rows(q, K, Vc, pos, out=o)
+        b.record()
+    torch.cuda.synchronize(dev)
+    us = statistics.median(a.elapsed_time(b) for a, b in ev) * 1e3
+    flops = 4.0 * net.D * net.Hq * float((pos + 1).sum().item())
+    peaks = load_peaks()
+    tf = flops / (us * 1e-6) / 1e12
+    return {"kernel": "attn_rows_tc_kernel<bf16>", "rows": R, "us_per_layer": round(us, 1),
+            "gflop_per_layer": round(flops / 1e9, 2), "tflops": round(tf, 1), "peak_tflops": peaks["bf16_tflops"],
+            "frac": round(tf / peaks["bf16_tflops"], 4), "peak_source": peaks["tc_source"]}
 
 
 def run_selector(args, dev, out_k, out_v, world):
@@ -373,9 +487,12 @@ def load_peaks():
     try:
         with open(p) as f:
             j = json.load(f)
-        return {"hbm_gbs": float(j["hbm_gbs"]), "source": "measured (MEASURED_PEAKS.json hbm_gbs)"}
+        return {"hbm_gbs": float(j["hbm_gbs"]), "source": "measured (MEASURED_PEAKS.json hbm_gbs)",
+                "bf16_tflops": float(j["bf16_tflops"]),
+                "tc_source": "measured burst (MEASURED_PEAKS.json bf16_tflops)"}
     except Exception:
-        return {"hbm_gbs": 6650.0, "source": "fallback 6.65 TB/s"}
+        return {"hbm_gbs": 6650.0, "source": "fallback 6.65 TB/s", "bf16_tflops": 1590.0,
+                "tc_source": "fallback 1.59 PFLOP/s"}
 
 
 def run_e2e(args, dev, pool_k, pool_v, ids, deltas, inv, world, rank):

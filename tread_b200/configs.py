@@ -40,12 +40,20 @@ def qwen2_config(arch, vocab=None, layers=None):
     return cfg
 
 
-def random_model(arch, dtype=torch.float32, device="cpu", seed=0, vocab=None, layers=None):
-    """Seeded random-init Qwen2ForCausalLM of architecture `arch` (init on CPU, then moved)."""
+def random_model(arch, dtype=torch.float32, device="cpu", seed=0, vocab=None, layers=None, init_on_device=False):
+    """Seeded random-init Qwen2ForCausalLM of architecture `arch`.
+
+    By default weights are drawn on the CPU (fp32, then cast and moved), so every process gets the
+    same weights. `init_on_device=True` draws them directly on `device` in `dtype` (seconds instead
+    of minutes for 7B+ architectures; reproducible on the same GPU model and torch build)."""
     from transformers import Qwen2ForCausalLM
 
     cfg = qwen2_config(arch, vocab=vocab, layers=layers)
     torch.manual_seed(seed)
+    if init_on_device:
+        with torch.device(device):
+            model = Qwen2ForCausalLM._from_config(cfg, dtype=dtype)
+        return model.eval()
     with torch.device("cpu"):
         model = Qwen2ForCausalLM(cfg)
     return model.to(dtype=dtype, device=device).eval()

@@ -49,6 +49,23 @@ class _Tmp:
         pass
 
 
+def _split_ids(segments, device):
+    """Host (CPU int64) and device views of a request's token-id segments with at most one
+    device->host and one host->device copy: block keys hash host ids, kernels read device ids.
+    The reference hashes each segment with its own blocking device->host copy (tread/store.py:26)."""
+    lens = [len(s) for s in segments]
+    if all(not s.is_cuda for s in segments):
+        host = [s.to(torch.int64) for s in segments]
+        flat = torch.cat(host)
+        if torch.cuda.is_available():
+            flat = flat.pin_memory()
+        dev_flat = flat.to(device, non_blocking=True)
+    else:
+        dev_flat = torch.cat([s.to(device=device, dtype=torch.int64) for s in segments])
+        host = list(dev_flat.cpu().split(lens))
+    return host, list(dev_flat.split(lens))
+
+
 class Engine:
     def __init__(self, model, store: BlockStore, graphs=False):
         self.model = model
@@ -76,14 +93,14 @@ class Engine:
         return K, V
 
     @torch.inference_mode()
-    def prefix_block(self, prefix_ids, st, namespace=""):
+    def prefix_block(self, prefix_ids, st, namespace="", host_ids=None):
         # Doc keys derive from this key, so a namespace isolates a tenant's whole block tree.
-        key = block_key(*self.sig, namespace, "prefix", prefix_ids)
+        key = block_key(*self.sig, namespace, "prefix", prefix_ids if host_ids is None else host_ids)
         b = self.store.get(key, wait=False)
         if b is None:
             st.misses += 1
             st.tokens_prefilled += len(prefix_ids)
-            K, V = self._prefill_rows(prefix_ids)
+            K, V = self._prefill_rows(prefix_ids.to(self.net.device))
             b = self.store.put(key, K, V, 0) or _Tmp(K, V, 0)
         else:
             st.hits += 1
@@ -91,13 +108,13 @@ class Engine:
         return key, b
 
     @torch.inference_mode()
-    def doc_blocks(self, prefix_key, pb, docs, st):
+    def doc_blocks(self, prefix_key, pb, docs, st, host_docs=None):
         """Look up every doc's block; prefill the misses after the cached prefix (tread/engine.py:59-96).
 
         Each missed doc runs at positions P.. over [prefix KV | its own KV], so it sees the prefix
         and itself, never another doc: the reference's block-diagonal packed prefill, per doc.
         """
-        keys = [block_key(*self.sig, prefix_key, d) for d in docs]
+        keys = [block_key(*self.sig, prefix_key, d) for d in (docs if host_docs is None else host_docs)]
         blocks = [self.store.get(k, wait=False) for k in keys]
         miss = [i for i, b in enumerate(blocks) if b is None]
         st.hits += len(docs) - len(miss)
@@ -109,7 +126,7 @@ class Engine:
         pb.wait()
         for i in miss:
             st.tokens_prefilled += len(docs[i])
-            Kf, Vf = self._prefill_rows(docs[i], (pb.K, pb.V), P)
+            Kf, Vf = self._prefill_rows(docs[i].to(self.net.device), (pb.K, pb.V), P)
             K, V = Kf[..., P:, :].contiguous(), Vf[..., P:, :].contiguous()
             blocks[i] = self.store.put(keys[i], K, V, P) or _Tmp(K, V, P)
         return blocks
@@ -126,8 +143,10 @@ class Engine:
         self._sync()
         t0 = time.perf_counter()
 
-        pkey, pb = self.prefix_block(prefix_ids, st, namespace)
-        blocks = self.doc_blocks(pkey, pb, docs, st)
+        host, devs = _split_ids([prefix_ids] + list(docs) + [query_ids], net.device)
+        prefix_ids, docs, query_ids = devs[0], devs[1:-1], devs[-1]
+        pkey, pb = self.prefix_block(prefix_ids, st, namespace, host_ids=host[0])
+        blocks = self.doc_blocks(pkey, pb, docs, st, host_docs=host[1:-1])
         P = pb.n_tokens
         nq = len(query_ids)
         T = P + sum(len(d) for d in docs)
@@ -195,7 +214,7 @@ class Engine:
         t0 = time.perf_counter()
         _, pb = self.prefix_block(prefix_ids, st)
         pb.wait()
-        rest = torch.cat(list(docs) + [query_ids])
+        rest = torch.cat(list(docs) + [query_ids]).to(self.net.device)
         st.tokens_prefilled += len(rest) - len(query_ids)
         P = pb.n_tokens
         K, V = self.net.new_cache(P + len(rest))
@@ -215,7 +234,7 @@ def prefill_full(model, prefix_ids, docs, query_ids):
     if torch.cuda.is_available():
         torch.cuda.synchronize()
     t0 = time.perf_counter()
-    ids = torch.cat([prefix_ids] + list(docs) + [query_ids])
+    ids = torch.cat([prefix_ids] + list(docs) + [query_ids]).to(net.device)
     K, V = net.new_cache(len(ids))
     Kl, Vl = list(K.unbind(0)), list(V.unbind(0))
     h = net.run(net.embed_ids(ids), torch.arange(len(ids), device=ids.device), Kl, Vl)

@@ -45,17 +45,25 @@ class Qwen2Rows:
         with torch.no_grad():
             for layer in model.model.layers:
                 a, m = layer.self_attn, layer.mlp
+                wqkv = torch.cat([a.q_proj.weight, a.k_proj.weight, a.v_proj.weight], 0).contiguous()
+                bqkv = torch.cat([a.q_proj.bias, a.k_proj.bias, a.v_proj.bias], 0).contiguous()
+                wgu = torch.cat([m.gate_proj.weight, m.up_proj.weight], 0).contiguous()
+                # The HF modules keep working on views of the packed tensors, so the packing costs
+                # no extra HBM (values are unchanged).
+                nq, nk = a.q_proj.weight.shape[0], a.k_proj.weight.shape[0]
+                a.q_proj.weight.data, a.k_proj.weight.data, a.v_proj.weight.data = (
+                    wqkv[:nq], wqkv[nq:nq + nk], wqkv[nq + nk:])
+                a.q_proj.bias.data, a.k_proj.bias.data, a.v_proj.bias.data = (
+                    bqkv[:nq], bqkv[nq:nq + nk], bqkv[nq + nk:])
+                inter = m.gate_proj.weight.shape[0]
+                m.gate_proj.weight.data, m.up_proj.weight.data = wgu[:inter], wgu[inter:]
                 self.layers.append(dict(
                     ln1=layer.input_layernorm.weight,
                     ln1_eps=layer.input_layernorm.variance_epsilon,
-                    wqkv=torch.cat([a.q_proj.weight, a.k_proj.weight, a.v_proj.weight], 0).contiguous(),
-                    bqkv=torch.cat([a.q_proj.bias, a.k_proj.bias, a.v_proj.bias], 0).contiguous(),
-                    wo=a.o_proj.weight,
+                    wqkv=wqkv, bqkv=bqkv, wo=a.o_proj.weight,
                     ln2=layer.post_attention_layernorm.weight,
                     ln2_eps=layer.post_attention_layernorm.variance_epsilon,
-                    wgu=torch.cat([m.gate_proj.weight, m.up_proj.weight], 0).contiguous(),
-                    wd=m.down_proj.weight,
-                    inter=m.gate_proj.weight.shape[0],
+                    wgu=wgu, wd=m.down_proj.weight, inter=inter,
                 ))
         self.err = torch.zeros(4, dtype=torch.int32, device=self.device)
 
@@ -89,11 +97,6 @@ class Qwen2Rows:
         gu = x @ p["wgu"].t()
         a = F.silu(gu[:, :p["inter"]]) * gu[:, p["inter"]:]
         return torch.addmm(h, a, p["wd"].t())
-
-    def layer1_kv(self, h):
-        """Layer-1 k (un-rotated k is never needed: rotated at the row position like the cache) and
-        v of rows h (layer-0 outputs): returns the packed qkv projection of layer 1."""
-        return self.qkv(1, h)
 
     def run(self, h, pos, Ks, Vs, l0=0, l1=None):
         for l in range(l0, self.L if l1 is None else l1):
