@@ -322,3 +322,31 @@ def test_tensor_core_attention_matches_fp32_reference(cuda, dtype, R, Hq, Hkv, T
     tol = 2e-2 if dtype == torch.bfloat16 else 4e-3
     torch.testing.assert_close(o[idx].float(), ref, rtol=0, atol=tol)
     torch.testing.assert_close(o.float(), o_cc.float(), rtol=0, atol=tol)
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+def test_tensor_core_attention_divergent_rescale(cuda, dtype):
+    """Within every warp, odd rows meet a score spike in a later key tile (their running max jumps
+    by far more than the rescale threshold) while even rows do not, so lanes of one warp disagree
+    on rescaling the TMEM accumulator."""
+    gen = torch.Generator(device=cuda).manual_seed(11)
+    R, Hq, Hkv, D, T = 256, 4, 2, 128, 640
+    u = torch.randn(D, device=cuda, generator=gen)
+    u = u / u.norm() * 4.0
+    q = torch.randn(R, Hq, D, device=cuda, generator=gen) * 0.5
+    q[1::2] += u
+    q[0::2] -= u
+    K = torch.randn(Hkv, T, D, device=cuda, generator=gen) * 0.5
+    V = torch.randn(Hkv, T, D, device=cuda, generator=gen)
+    K[:, 300] = 6.0 * u  # key tile 2: score ~ +96 * D^-0.5 for odd rows, ~ -96 for even rows
+    K[:, 520] = 9.0 * u  # and a second jump in tile 4
+    q, K, V = q.to(dtype), K.to(dtype), V.to(dtype)
+    pos = torch.full((R,), T - 1, device=cuda, dtype=torch.int64)
+    pos[::3] = torch.arange(0, R, 3, device=cuda) + 310  # some rows stop between the spikes
+    err = torch.zeros(4, dtype=torch.int32, device=cuda)
+    o = kernels.attn_rows(q, K, V, pos, err=err)
+    torch.cuda.synchronize()
+    assert err.max().item() == 0
+    ref = _sdpa_ref(q, K, V, pos)
+    tol = 2e-2 if dtype == torch.bfloat16 else 4e-3
+    torch.testing.assert_close(o.float(), ref, rtol=0, atol=tol)

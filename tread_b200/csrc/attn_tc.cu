@@ -39,7 +39,7 @@ constexpr int kKeys = 128;   // keys per step (MMA N of Q K^T, K of P V)
 constexpr int kD = 128;      // head_dim (MMA K of Q K^T, N of P V)
 constexpr int kBlock = 16384;  // one 128 x 64 bf16 swizzled block
 constexpr int kSmem = 8 * kBlock + 1024 + 128;
-constexpr long long kSpin = 1LL << 24;
+constexpr unsigned long long kWaitNs = 1000000000ull;  // 1 s: legitimate waits here take microseconds
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
@@ -66,11 +66,19 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t phase) {
   return ok != 0;
 }
 
-// Bounded wait: false if the phase did not complete within kSpin polls.
+__device__ __forceinline__ unsigned long long global_ns() {
+  unsigned long long t;
+  asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
+  return t;
+}
+
+// Bounded wait: false if the phase did not complete within kWaitNs of wall time.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t phase) {
-  for (long long i = 0; i < kSpin; ++i)
-    if (mbar_try_wait(bar, phase)) return true;
-  return false;
+  if (mbar_try_wait(bar, phase)) return true;
+  const unsigned long long t0 = global_ns();
+  while (!mbar_try_wait(bar, phase))
+    if (global_ns() - t0 > kWaitNs) return false;
+  return true;
 }
 
 __device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* map, uint64_t* bar, int x, int y, int z) {
@@ -267,21 +275,24 @@ __global__ void __launch_bounds__(128, 1)
     }
     const float m_new = fmaxf(m, tmax);
     const bool rescale = j > 0 && m_new > m + 8.f;
+    float alpha = 1.f;
     if (j == 0 || rescale) {
-      const float alpha = exp2f(m - m_new);  // 0 for the first step
+      alpha = exp2f(m - m_new);  // 0 for the first step
       l *= alpha;
-      if (rescale) {
-#pragma unroll 1
-        for (int c = 0; c < 4; ++c) {
-          float v[32];
-          tmem_ld32(tO + lane_off + c * 32, v);
-#pragma unroll
-          for (int i = 0; i < 32; ++i) v[i] *= alpha;
-          tmem_st32(tO + lane_off + c * 32, v);
-        }
-        asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
-      }
       m = m_new;
+    }
+    // tcgen05.ld / tcgen05.st are warp-collective (.sync.aligned): the O rows of a warp are
+    // rescaled together whenever any lane needs it, the other lanes multiplying by 1.
+    if (__any_sync(0xffffffffu, rescale)) {
+#pragma unroll 1
+      for (int c = 0; c < 4; ++c) {
+        float v[32];
+        tmem_ld32(tO + lane_off + c * 32, v);
+#pragma unroll
+        for (int i = 0; i < 32; ++i) v[i] *= alpha;
+        tmem_st32(tO + lane_off + c * 32, v);
+      }
+      asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
     }
     // P row -> shared memory, K-major 128B-swizzled: 16-byte chunk q of an 8-row atom row goes to q ^ (row % 8)
 #pragma unroll 1

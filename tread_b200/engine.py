@@ -192,6 +192,7 @@ class Engine:
             h = net.run(rows_h, rows_pos, Kl, Vl, start)
         self._sync()
         t2 = time.perf_counter()
+        net.check_errors()
 
         logits = net.logits(h[-1:])[0]
         cache = to_cache(Kl, Vl)
