@@ -4,21 +4,25 @@
 // forward of tread/engine.py:131-132): row r of head h attends to every cache key at a
 // position <= pos[r] of KV head h / (Hq/Hkv). This path covers bf16/fp16 with head_dim 128.
 //
-// One CTA (128 threads = one warpgroup) owns a tile of 128 consecutive rows of one query head:
-//   - TMA (128-byte swizzle) brings the Q tile once and a 128-key K tile and V tile per step
-//     into shared memory, straight from the [R, Hq, D] queries and the [Hkv, T, D] cache;
-//   - thread 0 issues S = Q K^T (M=128, N=128, K=128: 8 x tcgen05.mma kind::f16) into TMEM
-//     columns [0,128) and commits to an mbarrier;
-//   - each thread owns one row (= one TMEM lane): it reads its S row with tcgen05.ld, masks keys
-//     past its position, and keeps an online softmax in the exp2 domain. The output accumulator
-//     O lives in TMEM columns [128,256); it is rescaled (tcgen05.ld/st) only when the running
-//     max grows by more than 8 (log2 units) — a stale max is exact because the final 1/l uses
-//     the same max;
-//   - P (bf16) is written to shared memory in the canonical K-major 128B-swizzled layout and
-//     thread 0 issues O += P V (V as an MN-major B operand) into TMEM;
-//   - at the end each thread reads its O row, divides by l and stores it.
-// Every mbarrier wait is bounded; on timeout the CTA records bit 2 in *err, frees its TMEM and
-// returns.
+// One CTA owns a tile of 128 consecutive rows of one query head; the heaviest tiles (latest
+// positions, longest key ranges) are scheduled first. Roles and pipeline:
+//   - producer (lane 0 of warp 4): TMA (128-byte swizzle) loads the Q tile once and 128-key K/V
+//     tiles into a 2-stage ring straight from the [R, Hq, D] queries and the [Hkv, T, D] cache;
+//     it issues S_j = Q K_j^T (8 x tcgen05.mma kind::f16, M=N=K=128) into one of two TMEM S
+//     buffers, so the MMA of step j+1 runs while the rows are still in the softmax of step j,
+//     and O += P_j V_j into the TMEM accumulator once P_j is in shared memory;
+//   - softmax (warps 0-7; a row = a TMEM lane, its 128 columns split over two warps that swap
+//     partial maxima in shared memory): reads S once with tcgen05.ld into registers, masks keys
+//     past the row's position (only on tiles that reach it), keeps the running max and sum in
+//     the exp2 domain (ex2.approx, scale folded into one FMA), rescales O
+//     in TMEM only when the max grows by more than 8 (a stale max is exact since 1/l uses the
+//     same max; a warp rescales together because tcgen05.ld/st are warp-collective), and writes
+//     P (bf16/fp16) in the canonical K-major 128B-swizzled layout;
+//   - mbarriers hand off K/V stages, S buffers, P and PV completion between the roles.
+// TMEM: two 128-column S buffers + a 128-column O accumulator (512 allocated; one CTA per SM by
+// its shared memory). Every wait is bounded in wall time and aborts the whole CTA through a
+// shared flag; an aborted CTA records bit 2 in *err, lets issued copies and MMAs land, frees its
+// TMEM and returns.
 #include <cuda.h>
 
 #include <mutex>
@@ -38,7 +42,7 @@ constexpr int kRows = 128;   // query rows per CTA (MMA M)
 constexpr int kKeys = 128;   // keys per step (MMA N of Q K^T, K of P V)
 constexpr int kD = 128;      // head_dim (MMA K of Q K^T, N of P V)
 constexpr int kBlock = 16384;  // one 128 x 64 bf16 swizzled block
-constexpr int kSmem = 8 * kBlock + 1024 + 128;
+constexpr int kSmem = 12 * kBlock + 1024 + 128;
 constexpr unsigned long long kWaitNs = 1000000000ull;  // 1 s: legitimate waits here take microseconds
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
@@ -165,206 +169,281 @@ __host__ __device__ constexpr uint32_t idesc_f16(uint32_t fmt, uint32_t b_mn_maj
   return (1u << 4) | (fmt << 7) | (fmt << 10) | (b_mn_major << 16) | ((N >> 3) << 17) | ((M >> 4) << 24);
 }
 
+// Roles: warps 0-7 run the softmax: warp w covers TMEM lanes (rows) 32*(w%4).. and S/O columns
+// 64*(w/4).. of its row quadrant, so every row is shared by two warps that exchange their partial
+// max through shared memory; lane 0 of warp 8 is the producer that issues every TMA load and
+// every tcgen05.mma.
+constexpr int kSoftWarps = 8;
+constexpr int kThreadsTC = (kSoftWarps + 1) * 32;
+
+struct Waiter {
+  volatile int* abort;
+  // Bounded wait on an mbarrier phase; false if the CTA aborted or kWaitNs passed (then it aborts).
+  __device__ __forceinline__ bool operator()(uint64_t* bar, uint32_t parity) const {
+    if (mbar_try_wait(bar, parity)) return true;
+    const unsigned long long t0 = global_ns();
+    while (!mbar_try_wait(bar, parity)) {
+      if (*abort) return false;
+      if (global_ns() - t0 > kWaitNs) {
+        *abort = 1;
+        return false;
+      }
+    }
+    return true;
+  }
+};
+
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+
+// Barrier over the two softmax warps that share a row quadrant (named barrier 1 + quadrant).
+__device__ __forceinline__ void pair_sync(int quadrant) {
+  asm volatile("bar.sync %0, 64;" ::"r"(1 + quadrant) : "memory");
+}
+
+__device__ __forceinline__ float ex2(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
 template <typename T>
-__global__ void __launch_bounds__(128, 1)
+__global__ void __launch_bounds__(kThreadsTC, 1)
     attn_rows_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
                         const __grid_constant__ CUtensorMap tm_v, const int64_t* __restrict__ pos, int R, int Hq,
                         int G, long long T_cache, float scale_log2, T* __restrict__ out, unsigned* err) {
   extern __shared__ __align__(1024) unsigned char smem_raw[];
-  unsigned char* smem = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  unsigned char* smem =
+      reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   unsigned char* sQ = smem;               // 2 blocks: d 0-63, d 64-127
-  unsigned char* sK = smem + 2 * kBlock;  // 2 blocks
-  unsigned char* sV = smem + 4 * kBlock;  // 2 blocks
-  unsigned char* sP = smem + 6 * kBlock;  // 2 blocks: keys 0-63, 64-127
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + 8 * kBlock);  // [0] Q, [1] K/V, [2] MMA
-  uint32_t* s_tmem = reinterpret_cast<uint32_t*>(bars + 4);
-  int* s_flag = reinterpret_cast<int*>(bars + 5);
+  unsigned char* sK = smem + 2 * kBlock;  // 2 stages x 2 blocks
+  unsigned char* sV = smem + 6 * kBlock;  // 2 stages x 2 blocks
+  unsigned char* sP = smem + 10 * kBlock; // 2 blocks: keys 0-63, 64-127
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + 12 * kBlock);
+  uint64_t* q_full = bars + 0;
+  uint64_t* kv_full = bars + 1;  // [2]
+  uint64_t* s_full = bars + 3;   // [2]
+  uint64_t* s_free = bars + 5;   // [2]
+  uint64_t* p_full = bars + 7;
+  uint64_t* pv_done = bars + 8;
+  uint32_t* s_tmem = reinterpret_cast<uint32_t*>(bars + 9);
+  int* s_abort = reinterpret_cast<int*>(bars + 10);
+  __shared__ int s_wmax[4];
+  __shared__ float s_part[2][2][kRows];  // [step parity][column half][row]: partial max / final sum
 
-  const int tid = threadIdx.x, warp = tid >> 5;
-  const int h = blockIdx.y, g = h / G;
-  const int r0 = blockIdx.x * kRows;
-  const int row = r0 + tid;
-  const bool live = row < R;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int quad = warp & 3, half = (warp >> 2) & 1;
+  const int h = blockIdx.x, g = h / G;
+  const int tile = gridDim.y - 1 - blockIdx.y;  // latest rows (longest key ranges) start first
+  const int r0 = tile * kRows;
+  const int trow = quad * 32 + lane;  // row within the tile (= TMEM lane)
+  const int row = r0 + trow;
+  const bool soft = warp < kSoftWarps;
+  const bool live = soft && row < R;
   long long p = live ? pos[row] : 0;
   if (p < 0 || p >= T_cache) {
-    if (live && err) atomicOr(err, 2u);
+    if (live && half == 0 && err) atomicOr(err, 2u);
     p = 0;
   }
-  const int maxpos = __reduce_max_sync(0xffffffffu, (unsigned)p);
-  __shared__ int s_wmax[4];
-  if ((tid & 31) == 0) s_wmax[warp] = maxpos;
-
+  if (warp < 4) {
+    const int wm = __reduce_max_sync(0xffffffffu, (unsigned)p);
+    if (lane == 0) s_wmax[warp] = wm;
+  }
   if (warp == 0) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(s_tmem)),
-                 "r"(256)
+                 "r"(512)
                  : "memory");
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
   }
   if (tid == 0) {
-    mbar_init(&bars[0], 1);
-    mbar_init(&bars[1], 1);
-    mbar_init(&bars[2], 1);
-    *s_flag = 0;
+    mbar_init(q_full, 1);
+    mbar_init(&kv_full[0], 1);
+    mbar_init(&kv_full[1], 1);
+    mbar_init(&s_full[0], 1);
+    mbar_init(&s_full[1], 1);
+    mbar_init(&s_free[0], kSoftWarps * 32);
+    mbar_init(&s_free[1], kSoftWarps * 32);
+    mbar_init(p_full, kSoftWarps * 32);
+    mbar_init(pv_done, 1);
+    *s_abort = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *s_tmem;
-  const uint32_t tS = tmem, tO = tmem + 128;
-  const uint32_t lane_off = (uint32_t)(warp * 32) << 16;
   const int nsteps = max(max(s_wmax[0], s_wmax[1]), max(s_wmax[2], s_wmax[3])) / kKeys + 1;
+  const Waiter wait{s_abort};
 
-  constexpr uint32_t fmt = std::is_same<T, __nv_bfloat16>::value ? 1u : 0u;
-  constexpr uint32_t idesc_qk = idesc_f16(fmt, 0, kRows, kKeys);
-  constexpr uint32_t idesc_pv = idesc_f16(fmt, 1, kRows, kD);
-  const uint32_t aQ = smem_u32(sQ), aK = smem_u32(sK), aV = smem_u32(sV), aP = smem_u32(sP);
-
-  if (tid == 0) {
-    mbar_expect_tx(&bars[0], 2 * kBlock);
-    tma_load_3d(sQ, &tm_q, &bars[0], 0, h, r0);
-    tma_load_3d(sQ + kBlock, &tm_q, &bars[0], 64, h, r0);
-  }
-
-  float m = -INFINITY, l = 0.f;
-  bool ok = true;
-  uint32_t mma_phase = 0;
-#pragma unroll 1
-  for (int j = 0; j < nsteps && ok; ++j) {
-    if (tid == 0) {
-      mbar_expect_tx(&bars[1], 4 * kBlock);
-      tma_load_3d(sK, &tm_k, &bars[1], 0, j * kKeys, g);
-      tma_load_3d(sK + kBlock, &tm_k, &bars[1], 64, j * kKeys, g);
-      tma_load_3d(sV, &tm_v, &bars[1], 0, j * kKeys, g);
-      tma_load_3d(sV + kBlock, &tm_v, &bars[1], 64, j * kKeys, g);
+  if (!soft) {
+    // ------------------------------------------------------------------ producer (one lane)
+    if (lane == 0) {
+      constexpr uint32_t fmt = std::is_same<T, __nv_bfloat16>::value ? 1u : 0u;
+      constexpr uint32_t idesc_qk = idesc_f16(fmt, 0, kRows, kKeys);
+      constexpr uint32_t idesc_pv = idesc_f16(fmt, 1, kRows, kD);
+      const uint32_t aQ = smem_u32(sQ), aK = smem_u32(sK), aV = smem_u32(sV), aP = smem_u32(sP);
+      auto load_kv = [&](int j) {
+        const int s = j & 1;
+        mbar_expect_tx(&kv_full[s], 4 * kBlock);
+        tma_load_3d(sK + s * 2 * kBlock, &tm_k, &kv_full[s], 0, j * kKeys, g);
+        tma_load_3d(sK + s * 2 * kBlock + kBlock, &tm_k, &kv_full[s], 64, j * kKeys, g);
+        tma_load_3d(sV + s * 2 * kBlock, &tm_v, &kv_full[s], 0, j * kKeys, g);
+        tma_load_3d(sV + s * 2 * kBlock + kBlock, &tm_v, &kv_full[s], 64, j * kKeys, g);
+      };
+      auto issue_pv = [&](int j) {
+        const uint32_t vbase = aV + (j & 1) * 2 * kBlock;
+#pragma unroll
+        for (int k = 0; k < kKeys / 16; ++k)
+          mma_f16(tmem + 256, sw128_desc(aP + (k >> 2) * kBlock + (k & 3) * 32, 16, 1024),
+                  sw128_desc(vbase + k * 16 * 128, kBlock, 1024), idesc_pv, (j > 0 || k > 0) ? 1u : 0u);
+        mma_commit(pv_done);
+      };
+      mbar_expect_tx(q_full, 2 * kBlock);
+      tma_load_3d(sQ, &tm_q, q_full, 0, h, r0);
+      tma_load_3d(sQ + kBlock, &tm_q, q_full, 64, h, r0);
+      load_kv(0);
+      if (nsteps > 1) load_kv(1);
+      bool ok = true;
+      for (int j = 0; j < nsteps && ok; ++j) {
+        const int s = j & 1;
+        ok = wait(&kv_full[s], (j >> 1) & 1) && (j > 0 || wait(q_full, 0)) &&
+             (j < 2 || wait(&s_free[s], ((j - 2) >> 1) & 1));
+        if (!ok) break;
+        tc_fence_after();
+        const uint32_t kbase = aK + s * 2 * kBlock;
+#pragma unroll
+        for (int k = 0; k < kD / 16; ++k) {
+          const uint32_t off = (k >> 2) * kBlock + (k & 3) * 32;
+          mma_f16(tmem + s * 128, sw128_desc(aQ + off, 16, 1024), sw128_desc(kbase + off, 16, 1024), idesc_qk,
+                  k > 0);
+        }
+        mma_commit(&s_full[s]);
+        if (j >= 1) {
+          ok = wait(p_full, (j - 1) & 1);
+          if (!ok) break;
+          tc_fence_after();
+          issue_pv(j - 1);
+          if (j + 1 < nsteps) {
+            ok = wait(pv_done, (j - 1) & 1);  // stage (j+1)&1 was last read by QK(j-1) and PV(j-1)
+            if (!ok) break;
+            load_kv(j + 1);
+          }
+        }
+      }
+      if (ok && wait(p_full, (nsteps - 1) & 1)) {
+        tc_fence_after();
+        issue_pv(nsteps - 1);
+      }
     }
-    bool w = true;
-    if (j == 0) w = mbar_wait(&bars[0], 0);
-    w = w && mbar_wait(&bars[1], j & 1);
-    if (!__syncthreads_and(w)) {
-      ok = false;
-      break;
-    }
-    // S = Q K^T
-    if (tid == 0) {
+  } else {
+    // ------------------------------------------------------------------ softmax
+    const uint32_t lane_off = (uint32_t)(quad * 32) << 16;
+    const uint32_t col = half * 64;
+    const uint32_t tO = tmem + 256 + col;
+    float m = -INFINITY, l = 0.f;  // l: this half's partial row sum
+    bool ok = true;
+    for (int j = 0; j < nsteps; ++j) {
+      const int s = j & 1;
+      const uint32_t tS = tmem + s * 128 + col;
+      ok = __all_sync(0xffffffffu, wait(&s_full[s], (j >> 1) & 1));
+      if (!ok) break;
       tc_fence_after();
+      float v[64];
+      tmem_ld32(tS + lane_off, *reinterpret_cast<float(*)[32]>(v));
+      tmem_ld32(tS + lane_off + 32, *reinterpret_cast<float(*)[32]>(v + 32));
+      const long long key0 = (long long)j * kKeys + col;
+      if (__any_sync(0xffffffffu, key0 + 63 > p)) {
 #pragma unroll
-      for (int k = 0; k < kD / 16; ++k) {
-        const uint32_t off = (k >> 2) * kBlock + (k & 3) * 32;
-        mma_f16(tS, sw128_desc(aQ + off, 16, 1024), sw128_desc(aK + off, 16, 1024), idesc_qk, k > 0);
+        for (int i = 0; i < 64; ++i)
+          if (key0 + i > p) v[i] = -INFINITY;
       }
-      mma_commit(&bars[2]);
-    }
-    if (!__syncthreads_and(mbar_wait(&bars[2], mma_phase))) {
-      ok = false;
-      break;
-    }
-    mma_phase ^= 1;
-    tc_fence_after();
-
-    // online softmax over this row's 128 scores (exp2 domain)
-    const int key0 = j * kKeys;
-    float tmax = -INFINITY;
+      float tmax = v[0];
+#pragma unroll
+      for (int i = 1; i < 64; ++i) tmax = fmaxf(tmax, v[i]);
+      s_part[s][half][trow] = tmax * scale_log2;
+      pair_sync(quad);
+      const float m_new = fmaxf(m, fmaxf(tmax * scale_log2, s_part[s][half ^ 1][trow]));
+      const bool rescale = j > 0 && m_new > m + 8.f;
+      float alpha = 1.f;
+      if (j == 0 || rescale) {
+        alpha = ex2(m - m_new);  // 0 for the first step
+        l *= alpha;
+        m = m_new;
+      }
+      if (j > 0) {  // PV(j-1) done: P may be overwritten and O is stable
+        ok = __all_sync(0xffffffffu, wait(pv_done, (j - 1) & 1));
+        if (!ok) break;
+        tc_fence_after();
+      }
+      // tcgen05.ld/st are warp-collective: the warp rescales together, other lanes by 1
+      if (__any_sync(0xffffffffu, rescale)) {
 #pragma unroll 1
-    for (int c = 0; c < 4; ++c) {
-      float v[32];
-      tmem_ld32(tS + lane_off + c * 32, v);
+        for (int c = 0; c < 2; ++c) {
+          float o[32];
+          tmem_ld32(tO + lane_off + c * 32, o);
 #pragma unroll
-      for (int i = 0; i < 32; ++i)
-        if (key0 + c * 32 + i <= p) tmax = fmaxf(tmax, v[i] * scale_log2);
-    }
-    const float m_new = fmaxf(m, tmax);
-    const bool rescale = j > 0 && m_new > m + 8.f;
-    float alpha = 1.f;
-    if (j == 0 || rescale) {
-      alpha = exp2f(m - m_new);  // 0 for the first step
-      l *= alpha;
-      m = m_new;
-    }
-    // tcgen05.ld / tcgen05.st are warp-collective (.sync.aligned): the O rows of a warp are
-    // rescaled together whenever any lane needs it, the other lanes multiplying by 1.
-    if (__any_sync(0xffffffffu, rescale)) {
-#pragma unroll 1
-      for (int c = 0; c < 4; ++c) {
-        float v[32];
-        tmem_ld32(tO + lane_off + c * 32, v);
-#pragma unroll
-        for (int i = 0; i < 32; ++i) v[i] *= alpha;
-        tmem_st32(tO + lane_off + c * 32, v);
+          for (int i = 0; i < 32; ++i) o[i] *= alpha;
+          tmem_st32(tO + lane_off + c * 32, o);
+        }
+        asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
       }
-      asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
-    }
-    // P row -> shared memory, K-major 128B-swizzled: 16-byte chunk q of an 8-row atom row goes to q ^ (row % 8)
-#pragma unroll 1
-    for (int c = 0; c < 4; ++c) {
-      float v[32];
-      tmem_ld32(tS + lane_off + c * 32, v);
-      uint32_t pk[16];
+      // P row half -> shared memory block `half` (keys 64*half..), K-major 128B-swizzled:
+      // 16-byte chunk q of an 8-row atom row goes to q ^ (row % 8)
+      unsigned char* blk = sP + half * kBlock + (trow >> 3) * 1024 + (trow & 7) * 128;
 #pragma unroll
-      for (int i = 0; i < 32; i += 2) {
-        const float p0 = (key0 + c * 32 + i <= p) ? exp2f(v[i] * scale_log2 - m) : 0.f;
-        const float p1 = (key0 + c * 32 + i + 1 <= p) ? exp2f(v[i + 1] * scale_log2 - m) : 0.f;
-        l += p0 + p1;
-        pk[i / 2] = pack2<T>(p0, p1);
-      }
-      unsigned char* blk = sP + (c >> 1) * kBlock + (tid >> 3) * 1024 + (tid & 7) * 128;
+      for (int q = 0; q < 8; ++q) {
+        uint32_t pk[4];
 #pragma unroll
-      for (int q = 0; q < 4; ++q) {
-        const int chunk = (c & 1) * 4 + q;
-        *reinterpret_cast<uint4*>(blk + ((chunk ^ (tid & 7)) << 4)) =
-            make_uint4(pk[4 * q], pk[4 * q + 1], pk[4 * q + 2], pk[4 * q + 3]);
+        for (int i = 0; i < 8; i += 2) {
+          const float p0 = ex2(fmaf(v[q * 8 + i], scale_log2, -m));
+          const float p1 = ex2(fmaf(v[q * 8 + i + 1], scale_log2, -m));
+          l += p0 + p1;
+          pk[i / 2] = pack2<T>(p0, p1);
+        }
+        *reinterpret_cast<uint4*>(blk + ((q ^ (trow & 7)) << 4)) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
       }
+      tc_fence_before();
+      mbar_arrive(&s_free[s]);  // S buffer s fully read
+      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+      mbar_arrive(p_full);
     }
-    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-    tc_fence_before();
-    __syncthreads();
-    // O += P V
-    if (tid == 0) {
+    if (ok) ok = __all_sync(0xffffffffu, wait(pv_done, (nsteps - 1) & 1));
+    if (ok) {
       tc_fence_after();
-#pragma unroll
-      for (int k = 0; k < kKeys / 16; ++k) {
-        const uint32_t offp = (k >> 2) * kBlock + (k & 3) * 32;
-        const uint32_t offv = k * 16 * 128;  // 16 keys x 128 B per K step
-        mma_f16(tO, sw128_desc(aP + offp, 16, 1024), sw128_desc(aV + offv, kBlock, 1024), idesc_pv,
-                (j > 0 || k > 0) ? 1u : 0u);
-      }
-      mma_commit(&bars[2]);
-    }
-    if (!__syncthreads_and(mbar_wait(&bars[2], mma_phase))) {
-      ok = false;
-      break;
-    }
-    mma_phase ^= 1;
-    tc_fence_after();
-  }
-
-  if (ok) {
-    const float inv = 1.f / l;
-    T* orow = out + ((long long)row * Hq + h) * kD;
+      s_part[0][half][trow] = l;
+      pair_sync(quad);
+      const float inv = 1.f / (l + s_part[0][half ^ 1][trow]);
+      T* orow = out + ((long long)row * Hq + h) * kD + col;
 #pragma unroll 1
-    for (int c = 0; c < 4; ++c) {
-      float v[32];
-      tmem_ld32(tO + lane_off + c * 32, v);
-      if (live) {
+      for (int c = 0; c < 2; ++c) {
+        float o[32];
+        tmem_ld32(tO + lane_off + c * 32, o);
+        if (live) {
 #pragma unroll
-        for (int i = 0; i < 32; i += 8) {
-          uint4 o = make_uint4(pack2<T>(v[i] * inv, v[i + 1] * inv), pack2<T>(v[i + 2] * inv, v[i + 3] * inv),
-                               pack2<T>(v[i + 4] * inv, v[i + 5] * inv), pack2<T>(v[i + 6] * inv, v[i + 7] * inv));
-          *reinterpret_cast<uint4*>(orow + c * 32 + i) = o;
+          for (int i = 0; i < 32; i += 8) {
+            uint4 w = make_uint4(pack2<T>(o[i] * inv, o[i + 1] * inv), pack2<T>(o[i + 2] * inv, o[i + 3] * inv),
+                                 pack2<T>(o[i + 4] * inv, o[i + 5] * inv), pack2<T>(o[i + 6] * inv, o[i + 7] * inv));
+            *reinterpret_cast<uint4*>(orow + c * 32 + i) = w;
+          }
         }
       }
     }
-  } else if (tid == 0) {
-    if (err) atomicOr(err, 4u);
-    // let any TMA still in flight into our shared memory land before the CTA exits
-    mbar_wait(&bars[1], 0);
-    mbar_wait(&bars[1], 1);
   }
   tc_fence_before();
   __syncthreads();
+  if (*s_abort && tid == 0) {
+    if (err) atomicOr(err, 4u);
+    // let copies and MMAs already issued land before the CTA's resources go away
+    mbar_wait(pv_done, 0);
+    mbar_wait(pv_done, 1);
+    mbar_wait(&kv_full[0], 0);
+    mbar_wait(&kv_full[1], 0);
+  }
+  __syncthreads();
   if (warp == 0) {
     tc_fence_after();
-    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(256) : "memory");
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(512) : "memory");
   }
 }
 
@@ -423,8 +502,8 @@ int launch_tc(const void* q, const void* K, const void* V, long long c_sh, long 
   });
   TREAD_CHECK_CUDA(attr_rc);
   const float log2e = 1.4426950408889634f;
-  dim3 grid((R + kRows - 1) / kRows, Hq);
-  attn_rows_tc_kernel<T><<<grid, 128, kSmem, st>>>(mq, mk, mv, pos, R, Hq, Hq / Hkv, T_cache, sm_scale * log2e,
+  dim3 grid(Hq, (R + kRows - 1) / kRows);
+  attn_rows_tc_kernel<T><<<grid, kThreadsTC, kSmem, st>>>(mq, mk, mv, pos, R, Hq, Hq / Hkv, T_cache, sm_scale * log2e,
                                                    static_cast<T*>(out), err);
   TREAD_CHECK_LAUNCH("attn_rows_tc_kernel");
   return TREAD_OK;
