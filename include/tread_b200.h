@@ -168,6 +168,23 @@ int tread_attn_rows(const void* q, const void* K_cache, const void* V_cache, int
                     void* out, int dtype, int flags, void* err_flag, tread_stream_t stream);
 
 /*
+ * Fused RMSNorm over rows: y[r] = to_dtype(w * to_dtype(x[r] * rsqrt(mean(x[r]^2) + eps))), fp32
+ * inside. Replaces the HF Qwen2RMSNorm calls on the recomputed rows (tread/blend.py:105,113 via
+ * layer.input_layernorm / post_attention_layernorm), one pass instead of ~8 kernels.
+ * x, y: [rows, hidden] at row strides ld_x / ld_y (elements); weight [hidden]; 16-byte aligned.
+ */
+int tread_rmsnorm(const void* x, int64_t ld_x, const void* weight, void* y, int64_t ld_y, int64_t rows,
+                  int hidden, float eps, int dtype, tread_stream_t stream);
+
+/*
+ * Fused SwiGLU activation: y[r, i] = to_dtype(to_dtype(silu(g[r, i])) * u[r, i]) with
+ * gate_up[r] = [g | u] (2 * inter columns). Replaces act_fn(gate_proj(x)) * up_proj(x) of HF
+ * Qwen2MLP on the recomputed rows (tread/blend.py:113), one pass instead of two kernels.
+ */
+int tread_silu_mul(const void* gate_up, int64_t ld_gu, void* y, int64_t ld_y, int64_t rows, int inter,
+                   int dtype, tread_stream_t stream);
+
+/*
  * Block-store tier transfers (pinned host <-> HBM), stream-ordered DMA copies.
  *
  * tread_kv_spill replaces the GPU->CPU-tier move of tread/store.py:111

@@ -350,3 +350,24 @@ def test_tensor_core_attention_divergent_rescale(cuda, dtype):
     ref = _sdpa_ref(q, K, V, pos)
     tol = 2e-2 if dtype == torch.bfloat16 else 4e-3
     torch.testing.assert_close(o.float(), ref, rtol=0, atol=tol)
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16, torch.float32])
+def test_fused_rmsnorm_and_silu_mul_match_hf_modules(cuda, dtype):
+    """tread_rmsnorm / tread_silu_mul against HF Qwen2RMSNorm and SiLU(gate) * up on the same rows."""
+    from transformers.models.qwen2.modeling_qwen2 import Qwen2RMSNorm
+
+    gen = torch.Generator(device=cuda).manual_seed(4)
+    R, H, I = 333, 896, 4864
+    x = (torch.randn(R, H, device=cuda, generator=gen) * 3).to(dtype)
+    norm = Qwen2RMSNorm(H, eps=1e-6).to(cuda, dtype)
+    with torch.no_grad():
+        norm.weight.copy_(torch.randn(H, device=cuda, generator=gen))
+        ref = norm(x)
+    got = kernels.rmsnorm(x, norm.weight, 1e-6)
+    ulp = {torch.bfloat16: 2.0 ** -7, torch.float16: 2.0 ** -10, torch.float32: 2.0 ** -22}[dtype]
+    torch.testing.assert_close(got.float(), ref.float(), rtol=2 * ulp, atol=1e-6)
+    gu = (torch.randn(R, 2 * I, device=cuda, generator=gen) * 4).to(dtype)
+    ref2 = F.silu(gu[:, :I]) * gu[:, I:]
+    got2 = kernels.silu_mul(gu)
+    torch.testing.assert_close(got2.float(), ref2.float(), rtol=2 * ulp, atol=1e-6)

@@ -51,6 +51,8 @@ SIGNATURES = {
         [P, P, P, I64, I64, P, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int, F32, P, ctypes.c_int,
          ctypes.c_int, P, P],
     ),
+    "tread_rmsnorm": (ctypes.c_int, [P, I64, P, P, I64, I64, ctypes.c_int, F32, ctypes.c_int, P]),
+    "tread_silu_mul": (ctypes.c_int, [P, I64, P, I64, I64, ctypes.c_int, ctypes.c_int, P]),
     "tread_kv_fetch": (ctypes.c_int, [P, P, ctypes.c_size_t, P]),
     "tread_kv_spill": (ctypes.c_int, [P, P, ctypes.c_size_t, P]),
     "tread_kv_fetch_rows": (ctypes.c_int, [P, ctypes.c_size_t, P, ctypes.c_size_t, ctypes.c_size_t,

@@ -275,3 +275,35 @@ def attn_rows(q, K, V, pos, out=None, sm_scale=None, err=None, stream=None, cuda
                                      _stream_arg(stream, q.device))
     C.check(rc, "tread_attn_rows")
     return out
+
+
+# ---- fused row-wise layer pieces ----------------------------------------------------------------
+
+def rmsnorm(x, weight, eps, out=None, stream=None):
+    """HF Qwen2RMSNorm over the rows of x [R, H] (unit column stride) in one pass."""
+    C.require_cuda(x, "x")
+    if x.dim() != 2 or x.stride(1) != 1 or weight.shape != (x.shape[1],) or weight.dtype != x.dtype:
+        raise ValueError("rmsnorm: x must be [R, H] with unit column stride and weight [H] of x's dtype")
+    if out is None:
+        out = torch.empty_like(x, memory_format=torch.contiguous_format)
+    with torch.cuda.device(x.device):
+        rc = C.lib().tread_rmsnorm(x.data_ptr(), x.stride(0), weight.data_ptr(), out.data_ptr(), out.stride(0),
+                                   x.shape[0], x.shape[1], float(eps), C.dtype_code(x.dtype),
+                                   _stream_arg(stream, x.device))
+    C.check(rc, "tread_rmsnorm")
+    return out
+
+
+def silu_mul(gate_up, out=None, stream=None):
+    """silu(g) * u of HF Qwen2MLP, gate_up = [g | u] of shape [R, 2I] (unit column stride)."""
+    C.require_cuda(gate_up, "gate_up")
+    if gate_up.dim() != 2 or gate_up.stride(1) != 1 or gate_up.shape[1] % 2:
+        raise ValueError("silu_mul: gate_up must be [R, 2I] with unit column stride")
+    R, I = gate_up.shape[0], gate_up.shape[1] // 2
+    if out is None:
+        out = torch.empty(R, I, dtype=gate_up.dtype, device=gate_up.device)
+    with torch.cuda.device(gate_up.device):
+        rc = C.lib().tread_silu_mul(gate_up.data_ptr(), gate_up.stride(0), out.data_ptr(), out.stride(0), R, I,
+                                    C.dtype_code(gate_up.dtype), _stream_arg(stream, gate_up.device))
+    C.check(rc, "tread_silu_mul")
+    return out

@@ -5,10 +5,10 @@ The reference drives HF's Qwen2 modules directly (tread/blend.py:82-114, tread/e
 that every path the hot path needs is one primitive: a set of token rows, each at its own
 absolute position, runs through layers [l0, l1) against per-layer KV caches, with
 
-    x = RMSNorm(h);  qkv = x @ Wqkv^T + b            (one GEMM, cuBLAS)
-    RoPE(q, k at pos) ; K[pos], V[pos] = k, v        (tread_rope_rows)
-    o = attention(q, K, V, key_pos <= pos)           (tread_attn_rows)
-    h = h + o @ Wo^T ; h = h + down(silu(gate) * up) (GEMMs; SwiGLU)
+    x = RMSNorm(h) (tread_rmsnorm);  qkv = x @ Wqkv^T + b  (one GEMM, cuBLAS)
+    RoPE(q, k at pos) ; K[pos], V[pos] = k, v              (tread_rope_rows)
+    o = attention(q, K, V, key_pos <= pos)                 (tread_attn_rows)
+    h = h + o @ Wo^T ; h = h + down(silu(gate) * up)       (GEMMs; tread_silu_mul)
 
 Rows are: recomputed tokens (blend), the query segment, a prefix or a doc being prefilled.
 A row only ever sees keys at positions <= its own, which is the causal mask of a prefill, the
@@ -67,12 +67,10 @@ class Qwen2Rows:
                 ))
         self.err = torch.zeros(4, dtype=torch.int32, device=self.device)
 
-    # -- elementwise pieces (HF Qwen2RMSNorm / SwiGLU semantics) --------------------------------
+    # -- elementwise pieces (HF Qwen2RMSNorm / SwiGLU semantics, fused kernels) ------------------
     @staticmethod
     def rmsnorm(x, w, eps):
-        x32 = x.float()
-        var = x32.pow(2).mean(-1, keepdim=True)
-        return w * (x32 * torch.rsqrt(var + eps)).to(x.dtype)
+        return kernels.rmsnorm(x, w, eps)
 
     def embed_ids(self, ids):
         return F.embedding(ids, self.embed)
@@ -84,7 +82,8 @@ class Qwen2Rows:
 
     def layer(self, l, h, pos, K, V, qkv=None):
         """h: [R, hidden] rows at positions pos (int64 [R]); K, V: layer-l caches [1, Hkv, T, D]
-        (or [Hkv, T, D]); the rows' k/v are written into them. Returns the new h."""
+        (or [Hkv, T, D]); the rows' k/v are written into them. The residual stream is updated in
+        place (h is returned)."""
         p = self.layers[l]
         R = h.shape[0]
         if qkv is None:
@@ -92,13 +91,14 @@ class Qwen2Rows:
         q = torch.empty(R, self.Hq, self.D, dtype=h.dtype, device=h.device)
         kernels.rope_rows(qkv, pos, self.Hq, self.Hkv, self.D, q, K, V, self.inv_freq, self.attn_scaling, self.err)
         o = kernels.attn_rows(q, K, V, pos, err=self.err)
-        h = torch.addmm(h, o.view(R, -1), p["wo"].t())
+        h.addmm_(o.view(R, -1), p["wo"].t())
         x = self.rmsnorm(h, p["ln2"], p["ln2_eps"])
-        gu = x @ p["wgu"].t()
-        a = F.silu(gu[:, :p["inter"]]) * gu[:, p["inter"]:]
-        return torch.addmm(h, a, p["wd"].t())
+        a = kernels.silu_mul(x @ p["wgu"].t())
+        return h.addmm_(a, p["wd"].t())
 
     def run(self, h, pos, Ks, Vs, l0=0, l1=None):
+        """Rows h through layers [l0, l1); returns the final hidden rows (h itself is not modified)."""
+        h = h.clone()
         for l in range(l0, self.L if l1 is None else l1):
             h = self.layer(l, h, pos, Ks[l], Vs[l])
         return h
