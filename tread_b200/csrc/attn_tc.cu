@@ -6,8 +6,9 @@
 //
 // One CTA owns a tile of 128 consecutive rows of one query head; the heaviest tiles (latest
 // positions, longest key ranges) are scheduled first. Roles and pipeline:
-//   - producer (lane 0 of warp 4): TMA (128-byte swizzle) loads the Q tile once and 128-key K/V
-//     tiles into a 2-stage ring straight from the [R, Hq, D] queries and the [Hkv, T, D] cache;
+//   - producer (lane 0 of warp 8): TMA (128-byte swizzle) loads the Q tile once and 128-key K and
+//     V tiles into separate 2-stage rings (K two steps ahead of QK, V two steps ahead of PV)
+//     straight from the [R, Hq, D] queries and the [Hkv, T, D] cache;
 //     it issues S_j = Q K_j^T (8 x tcgen05.mma kind::f16, M=N=K=128) into one of two TMEM S
 //     buffers, so the MMA of step j+1 runs while the rows are still in the softmax of step j,
 //     and O += P_j V_j into the TMEM accumulator once P_j is in shared memory;
@@ -222,13 +223,14 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
   unsigned char* sP = smem + 10 * kBlock; // 2 blocks: keys 0-63, 64-127
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + 12 * kBlock);
   uint64_t* q_full = bars + 0;
-  uint64_t* kv_full = bars + 1;  // [2]
-  uint64_t* s_full = bars + 3;   // [2]
-  uint64_t* s_free = bars + 5;   // [2]
-  uint64_t* p_full = bars + 7;
-  uint64_t* pv_done = bars + 8;
-  uint32_t* s_tmem = reinterpret_cast<uint32_t*>(bars + 9);
-  int* s_abort = reinterpret_cast<int*>(bars + 10);
+  uint64_t* k_full = bars + 1;   // [2]
+  uint64_t* v_full = bars + 3;   // [2]
+  uint64_t* s_full = bars + 5;   // [2]
+  uint64_t* s_free = bars + 7;   // [2]
+  uint64_t* p_full = bars + 9;
+  uint64_t* pv_done = bars + 10;
+  uint32_t* s_tmem = reinterpret_cast<uint32_t*>(bars + 11);
+  int* s_abort = reinterpret_cast<int*>(bars + 12);
   __shared__ int s_wmax[4];
   __shared__ float s_part[2][2][kRows];  // [step parity][column half][row]: partial max / final sum
 
@@ -258,8 +260,10 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
   }
   if (tid == 0) {
     mbar_init(q_full, 1);
-    mbar_init(&kv_full[0], 1);
-    mbar_init(&kv_full[1], 1);
+    mbar_init(&k_full[0], 1);
+    mbar_init(&k_full[1], 1);
+    mbar_init(&v_full[0], 1);
+    mbar_init(&v_full[1], 1);
     mbar_init(&s_full[0], 1);
     mbar_init(&s_full[1], 1);
     mbar_init(&s_free[0], kSoftWarps * 32);
@@ -283,13 +287,19 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
       constexpr uint32_t idesc_qk = idesc_f16(fmt, 0, kRows, kKeys);
       constexpr uint32_t idesc_pv = idesc_f16(fmt, 1, kRows, kD);
       const uint32_t aQ = smem_u32(sQ), aK = smem_u32(sK), aV = smem_u32(sV), aP = smem_u32(sP);
-      auto load_kv = [&](int j) {
+      // K and V have separate 2-stage rings: K(j+2) is fetched as soon as QK(j) has read its
+      // stage, V(j+1) as soon as PV(j-1) has, so copies run two steps ahead of the MMAs.
+      auto load_k = [&](int j) {
         const int s = j & 1;
-        mbar_expect_tx(&kv_full[s], 4 * kBlock);
-        tma_load_3d(sK + s * 2 * kBlock, &tm_k, &kv_full[s], 0, j * kKeys, g);
-        tma_load_3d(sK + s * 2 * kBlock + kBlock, &tm_k, &kv_full[s], 64, j * kKeys, g);
-        tma_load_3d(sV + s * 2 * kBlock, &tm_v, &kv_full[s], 0, j * kKeys, g);
-        tma_load_3d(sV + s * 2 * kBlock + kBlock, &tm_v, &kv_full[s], 64, j * kKeys, g);
+        mbar_expect_tx(&k_full[s], 2 * kBlock);
+        tma_load_3d(sK + s * 2 * kBlock, &tm_k, &k_full[s], 0, j * kKeys, g);
+        tma_load_3d(sK + s * 2 * kBlock + kBlock, &tm_k, &k_full[s], 64, j * kKeys, g);
+      };
+      auto load_v = [&](int j) {
+        const int s = j & 1;
+        mbar_expect_tx(&v_full[s], 2 * kBlock);
+        tma_load_3d(sV + s * 2 * kBlock, &tm_v, &v_full[s], 0, j * kKeys, g);
+        tma_load_3d(sV + s * 2 * kBlock + kBlock, &tm_v, &v_full[s], 64, j * kKeys, g);
       };
       auto issue_pv = [&](int j) {
         const uint32_t vbase = aV + (j & 1) * 2 * kBlock;
@@ -302,12 +312,16 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
       mbar_expect_tx(q_full, 2 * kBlock);
       tma_load_3d(sQ, &tm_q, q_full, 0, h, r0);
       tma_load_3d(sQ + kBlock, &tm_q, q_full, 64, h, r0);
-      load_kv(0);
-      if (nsteps > 1) load_kv(1);
+      load_k(0);
+      load_v(0);
+      if (nsteps > 1) {
+        load_k(1);
+        load_v(1);
+      }
       bool ok = true;
       for (int j = 0; j < nsteps && ok; ++j) {
         const int s = j & 1;
-        ok = wait(&kv_full[s], (j >> 1) & 1) && (j > 0 || wait(q_full, 0)) &&
+        ok = wait(&k_full[s], (j >> 1) & 1) && (j > 0 || wait(q_full, 0)) &&
              (j < 2 || wait(&s_free[s], ((j - 2) >> 1) & 1));
         if (!ok) break;
         tc_fence_after();
@@ -320,18 +334,23 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
         }
         mma_commit(&s_full[s]);
         if (j >= 1) {
-          ok = wait(p_full, (j - 1) & 1);
+          ok = wait(p_full, (j - 1) & 1) && wait(&v_full[(j - 1) & 1], ((j - 1) >> 1) & 1);
           if (!ok) break;
           tc_fence_after();
           issue_pv(j - 1);
-          if (j + 1 < nsteps) {
-            ok = wait(pv_done, (j - 1) & 1);  // stage (j+1)&1 was last read by QK(j-1) and PV(j-1)
-            if (!ok) break;
-            load_kv(j + 1);
-          }
+        }
+        if (j + 2 < nsteps) {
+          ok = wait(&s_full[s], (j >> 1) & 1);  // QK(j) has read K stage s
+          if (!ok) break;
+          load_k(j + 2);
+        }
+        if (j >= 1 && j + 1 < nsteps) {
+          ok = wait(pv_done, (j - 1) & 1);  // PV(j-1) has read V stage (j+1)&1
+          if (!ok) break;
+          load_v(j + 1);
         }
       }
-      if (ok && wait(p_full, (nsteps - 1) & 1)) {
+      if (ok && wait(p_full, (nsteps - 1) & 1) && wait(&v_full[(nsteps - 1) & 1], ((nsteps - 1) >> 1) & 1)) {
         tc_fence_after();
         issue_pv(nsteps - 1);
       }
@@ -435,10 +454,13 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
   if (*s_abort && tid == 0) {
     if (err) atomicOr(err, 4u);
     // let copies and MMAs already issued land before the CTA's resources go away
-    mbar_wait(pv_done, 0);
-    mbar_wait(pv_done, 1);
-    mbar_wait(&kv_full[0], 0);
-    mbar_wait(&kv_full[1], 0);
+    for (int b = 0; b < 2; ++b) {
+      mbar_wait(pv_done, b);
+      mbar_wait(&k_full[0], b);
+      mbar_wait(&k_full[1], b);
+      mbar_wait(&v_full[0], b);
+      mbar_wait(&v_full[1], b);
+    }
   }
   __syncthreads();
   if (warp == 0) {
