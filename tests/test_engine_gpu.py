@@ -180,6 +180,10 @@ def test_cuda_graph_blend_matches_eager(tiny, req, policy, ratio):
     # the query rows of the ratio-0 requests above already use the runner, so a blended request
     # may land in a bucket captured by them; what must hold is that a repeat captures nothing
     b, _, _ = graphed.prefill(prefix, docs[::-1], query, ratio=ratio, policy=policy)
+    # churn the caching allocator: memory the graph still reads must not be handed out again
+    # (zeros, so a violation shows up as a wrong result, not an out-of-range index)
+    junk = [torch.zeros(n, dtype=torch.int64, device=prefix.device) for n in range(1, 600, 7) for _ in range(3)]
+    del junk
     before = graphed.runner.captures
     b, _, _ = graphed.prefill(prefix, docs[::-1], query, ratio=ratio, policy=policy)
     assert graphed.runner.captures == before and 1 <= before <= 2

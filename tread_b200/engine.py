@@ -15,7 +15,11 @@ B200 changes inside `prefill`:
     read per layer), and with ratio 0 they are the only rows: every row attends to the keys at
     positions <= its own, which reproduces blend-then-query exactly;
   - stage timers keep the reference's names: `blend` covers the layer pass (recompute rows and
-    query rows), `query` the final norm + lm_head and the cache handle.
+    query rows) and the first-token logits, `query` the cache handle;
+  - with graphs=True everything after assembly (selection, layers, logits) replays as one CUDA
+    graph per request shape, and the request cache is that graph's static buffer, assembled in
+    place: the returned cache is valid until the next request of the same shape (as the
+    reference's graphed runner returns views of its static buffers, tread/graphs.py:8-13).
 """
 import time
 from dataclasses import dataclass, field
@@ -24,7 +28,7 @@ import torch
 
 from tread_b200 import kernels
 from tread_b200.blend import rows_of, select, to_cache
-from tread_b200.graphs import SubsetRunner
+from tread_b200.graphs import RequestGraph, SubsetRunner
 from tread_b200.store import BlockStore, block_key
 
 
@@ -150,7 +154,16 @@ class Engine:
         P = pb.n_tokens
         nq = len(query_ids)
         T = P + sum(len(d) for d in docs)
-        K, V = self._request_cache(T + nq)
+        graph = None
+        if self.runner is not None and (policy != "random" or ratio == 0):
+            # the request's cache is the graph's static buffer: assembled in place, nothing copied
+            lens = tuple(len(d) for d in docs)
+            graph = self.runner.request_graph(
+                (P, lens, nq, ratio, policy),
+                lambda: RequestGraph(self._compute, self.net, P, lens, nq, ratio, policy))
+            K, V = graph.K, graph.V
+        else:
+            K, V = self._request_cache(T + nq)
         segs, pending, cands = [(pb, 0, 0)], [], []
         offset = P
         for d, b in zip(docs, blocks):
@@ -165,15 +178,37 @@ class Engine:
                     b.wait()
                 kernels.rope_gather_append([(b.K, b.V, dl, o) for b, dl, o in group], K, V, net.inv_freq,
                                            net.attn_scaling)
-        Kl, Vl = list(K.unbind(0)), list(V.unbind(0))
         self._sync()
         t1 = time.perf_counter()
 
+        ctx = torch.cat([prefix_ids] + list(docs))
+        if graph is not None:
+            graph.ctx.copy_(ctx)
+            graph.q.copy_(query_ids)
+            graph.graph.replay()
+            logits, st.recompute_eff = graph.logits.clone(), graph.eff
+        else:
+            logits, st.recompute_eff = self._compute(K, V, ctx, query_ids, cands, T, nq, ratio, policy)
+        self._sync()
+        t2 = time.perf_counter()
+        net.check_errors()
+
+        cache = to_cache(list(K.unbind(0)), list(V.unbind(0)))
+        self._sync()
+        t3 = time.perf_counter()
+        st.t = dict(assemble=t1 - t0, blend=t2 - t1, query=t3 - t2, ttft=t3 - t0)
+        return logits, cache, st
+
+    def _compute(self, K, V, ctx, query_ids, cands, T, nq, ratio, policy):
+        """Everything after assembly, with no host synchronisation (so it can be graph-captured):
+        token selection, the recompute + query rows through the layers, first-token logits.
+        Returns (logits [vocab], effective recompute ratio)."""
+        net = self.net
+        Kl, Vl = list(K.unbind(0)), list(V.unbind(0))
         hq = net.embed_ids(query_ids)
         qpos = torch.arange(T, T + nq, device=query_ids.device)
-        start, rows_h, rows_pos = 0, hq, qpos
+        start, rows_h, rows_pos, eff = 0, hq, qpos, 0.0
         if ratio > 0 and cands:
-            ctx = torch.cat([prefix_ids] + list(docs))
             S, hS, start, all_c, hx = select(self.model, ctx, Kl, Vl, cands, ratio, policy, inplace=True,
                                              extra=(hq, qpos))
             if len(S):
@@ -183,23 +218,11 @@ class Engine:
                     hq = hx  # query rows already went through layer 0 with the candidates
                 rows_h, rows_pos = torch.cat([hS, hq]), torch.cat([S, qpos])
                 n, L = len(all_c), net.L
-                st.recompute_eff = (len(S) * (L - start) + start * n) / (n * L)
+                eff = (len(S) * (L - start) + start * n) / (n * L)
             else:
                 start = 0
-        if self.runner is not None and self.runner.worth_it(T + nq):
-            h = self.runner.run_rows(rows_h, rows_pos, Kl, Vl, start)
-        else:
-            h = net.run(rows_h, rows_pos, Kl, Vl, start)
-        self._sync()
-        t2 = time.perf_counter()
-        net.check_errors()
-
-        logits = net.logits(h[-1:])[0]
-        cache = to_cache(Kl, Vl)
-        self._sync()
-        t3 = time.perf_counter()
-        st.t = dict(assemble=t1 - t0, blend=t2 - t1, query=t3 - t2, ttft=t3 - t0)
-        return logits, cache, st
+        h = net.run(rows_h, rows_pos, Kl, Vl, start)
+        return net.logits(h[-1:])[0], eff
 
     def _request_cache(self, T):
         shape = (self.net.L, 1, self.net.Hkv, T, self.net.D)

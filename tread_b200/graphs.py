@@ -47,7 +47,8 @@ class _Graph:
 
 
 class SubsetRunner:
-    """Caches one graph per (start layer, bucket); keeps at most `max_graphs` (LRU)."""
+    """Caches one graph per (start layer, bucket); keeps at most `max_graphs` (LRU). The engine
+    also keeps its whole-request graphs (RequestGraph) here, under the same LRU limit."""
 
     def __init__(self, model, max_graphs=4, max_ctx=2048):
         self.model = model
@@ -61,6 +62,18 @@ class SubsetRunner:
 
     def worth_it(self, T):
         return T <= self.max_ctx
+
+    def request_graph(self, key, build):
+        key = ("request",) + tuple(key)
+        g = self.graphs.get(key)
+        if g is None:
+            while len(self.graphs) >= self.max_graphs:
+                self.graphs.popitem(last=False)
+            g = build()
+            self.graphs[key] = g
+            self.captures += 1
+        self.graphs.move_to_end(key)
+        return g
 
     def _graph(self, n, T, start):
         nb, Tb = _bucket(n, T)
@@ -104,3 +117,36 @@ class SubsetRunner:
         """Engine path: rows h at positions pos through layers start..L-1 of the full per-layer
         cache lists Kl/Vl (updated in place). Returns the rows' final hidden states."""
         return self._replay(h, pos, Kl[start:], Vl[start:], start, Kl[0].shape[-2])
+
+
+class RequestGraph:
+    """Everything after assembly for one request shape (prefix length, doc lengths, query length,
+    ratio, policy), captured as one CUDA graph over static buffers: the request KV cache (which
+    the engine assembles into directly), the context and query token ids, and the logits."""
+
+    def __init__(self, compute, net, P, doc_lens, nq, ratio, policy):
+        T = P + sum(doc_lens)
+        shape = (net.L, 1, net.Hkv, T + nq, net.D)
+        self.K = torch.zeros(shape, dtype=net.dtype, device=net.device)
+        self.V = torch.zeros_like(self.K)
+        self.ctx = torch.zeros(T, dtype=torch.int64, device=net.device)
+        self.q = torch.zeros(nq, dtype=torch.int64, device=net.device)
+        # Every tensor the captured kernels read must outlive the graph: keep them on self.
+        self.cands, off = [], P
+        for n in doc_lens:
+            self.cands.append(torch.arange(off, off + n, device=net.device))
+            off += n
+
+        def body():
+            return compute(self.K, self.V, self.ctx, self.q, self.cands, T, nq, ratio, policy)
+
+        s = torch.cuda.Stream(device=net.device)
+        s.wait_stream(torch.cuda.current_stream(net.device))
+        with torch.cuda.stream(s):
+            for _ in range(2):
+                body()
+        torch.cuda.current_stream(net.device).wait_stream(s)
+        self.graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(self.graph):
+            self.logits, self.eff = body()
+        net.err.zero_()  # the warm-up ran on an all-zero cache
