@@ -53,6 +53,8 @@ def parse():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=10.0, help="CPU baseline sample budget")
     ap.add_argument("--no-ttft", action="store_true", help="skip the configs[2] 7B TTFT leg")
+    ap.add_argument("--only", choices=["attention", "selector"], default=None,
+                    help="run one kernel microbench alone (for profiler captures) and print its timing")
     ap.add_argument("--ttft-reps", type=int, default=5, help="timed warm requests per recompute ratio")
     return ap.parse_args()
 
@@ -569,10 +571,54 @@ def run_e2e(args, dev, pool_k, pool_v, ids, deltas, inv, world, rank):
             "path": "pinned host blocks -> tread_kv_fetch -> tread_rope_gather_append -> tread_kv_spill_rows"}
 
 
+def run_only(args):
+    """One kernel alone on configs[2]/[1] shapes, --warmup + --steps launches (profiler captures)."""
+    from tread_b200 import kernels
+
+    dev = torch.device("cuda", 0)
+    gen = torch.Generator(device=dev).manual_seed(args.seed)
+    T_ctx, nq, Hq = 16 * 496 + 256, 64, 28
+    if args.only == "attention":
+        # one layer of a 20% request: 1587 selected positions + 64 query rows vs 8256 cached keys
+        S = torch.sort(torch.randperm(T_ctx - 256, device=dev, generator=gen)[:1587]).values + 256
+        pos = torch.cat([S, torch.arange(T_ctx, T_ctx + nq, device=dev)])
+        q = torch.randn(len(pos), Hq, D, device=dev, generator=gen).to(torch.bfloat16)
+        K = torch.randn(HKV, T_ctx + nq, D, device=dev, generator=gen).to(torch.bfloat16)
+        V = torch.randn_like(K)
+        out = torch.empty_like(q)
+        run = lambda: kernels.attn_rows(q, K, V, pos, out=out)
+        flops = 4.0 * D * Hq * float((pos + 1).sum().item())
+    else:
+        n = 8192
+        K1 = torch.randn(HKV, n, D, device=dev, generator=gen).to(torch.bfloat16)
+        V1 = torch.randn_like(K1)
+        k1 = (K1.float() + 0.05 * torch.randn(K1.shape, device=dev, generator=gen)).to(torch.bfloat16)
+        v1 = (V1.float() + 0.05 * torch.randn(V1.shape, device=dev, generator=gen)).to(torch.bfloat16)
+        cand = torch.arange(n, device=dev)
+        run = lambda: kernels.deviation_topk(k1, v1, K1, V1, cand, 1638)
+        flops = None
+    for _ in range(args.warmup):
+        run()
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
+    for a, b in ev:
+        a.record()
+        run()
+        b.record()
+    torch.cuda.synchronize(dev)
+    us = statistics.median(a.elapsed_time(b) for a, b in ev) * 1e3
+    line = {"only": args.only, "us_per_call": round(us, 2)}
+    if flops:
+        line["tflops"] = round(flops / (us * 1e-6) / 1e12, 1)
+    print(json.dumps(line), flush=True)
+    return 0
+
+
 def main():
     args = parse()
     if args.impl == "reference":
         return run_reference(args)
+    if args.only:
+        return run_only(args)
     return run_gpu(args)
 
 

@@ -6,10 +6,12 @@
 //
 // One CTA owns a tile of 128 consecutive rows of one query head; the heaviest tiles (latest
 // positions, longest key ranges) are scheduled first. Roles and pipeline:
-//   - producer (lane 0 of warp 8): TMA (128-byte swizzle) loads the Q tile once and 128-key K and
-//     V tiles into separate 2-stage rings (K two steps ahead of QK, V two steps ahead of PV)
-//     straight from the [R, Hq, D] queries and the [Hkv, T, D] cache;
-//     it issues S_j = Q K_j^T (8 x tcgen05.mma kind::f16, M=N=K=128) into one of two TMEM S
+//   - loader (lane 0 of warp 9): TMA (128-byte swizzle) loads the Q tile once and 128-key K and V
+//     tiles into separate 2-stage rings (two steps ahead of the MMAs that read them) straight
+//     from the [R, Hq, D] queries and the [Hkv, T, D] cache, refilling a stage when the MMA that
+//     read it commits to that stage's "free" barrier;
+//   - MMA issuer (lane 0 of warp 8): issues
+//     S_j = Q K_j^T (8 x tcgen05.mma kind::f16, M=N=K=128) into one of two TMEM S
 //     buffers, so the MMA of step j+1 runs while the rows are still in the softmax of step j,
 //     and O += P_j V_j into the TMEM accumulator once P_j is in shared memory;
 //   - softmax (warps 0-7; a row = a TMEM lane, its 128 columns split over two warps that swap
@@ -43,8 +45,12 @@ constexpr int kRows = 128;   // query rows per CTA (MMA M)
 constexpr int kKeys = 128;   // keys per step (MMA N of Q K^T, K of P V)
 constexpr int kD = 128;      // head_dim (MMA K of Q K^T, N of P V)
 constexpr int kBlock = 16384;  // one 128 x 64 bf16 swizzled block
-constexpr int kSmem = 12 * kBlock + 1024 + 128;
+constexpr int kSmem = 10 * kBlock + 1024 + 256;
 constexpr unsigned long long kWaitNs = 1000000000ull;  // 1 s: legitimate waits here take microseconds
+constexpr unsigned long long kAbortWaitNs = 20000000ull;  // 20 ms per barrier phase on the abort path
+// TMEM columns: S buffers 0-127 and 128-255 (fp32), O 256-383 (fp32), P buffers 384-447 and
+// 448-511 (bf16/fp16 pairs).
+constexpr uint32_t kTmemO = 256, kTmemP = 384;
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
@@ -78,11 +84,11 @@ __device__ __forceinline__ unsigned long long global_ns() {
 }
 
 // Bounded wait: false if the phase did not complete within kWaitNs of wall time.
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t phase) {
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t phase, unsigned long long limit_ns) {
   if (mbar_try_wait(bar, phase)) return true;
   const unsigned long long t0 = global_ns();
   while (!mbar_try_wait(bar, phase))
-    if (global_ns() - t0 > kWaitNs) return false;
+    if (global_ns() - t0 > limit_ns) return false;
   return true;
 }
 
@@ -110,6 +116,17 @@ __device__ __forceinline__ void mma_f16(uint32_t tmem_d, uint64_t a, uint64_t b,
       : "memory");
 }
 
+// Same with A (M x K, 16-bit elements packed two per 32-bit column, row = TMEM lane) in TMEM.
+__device__ __forceinline__ void mma_f16_ts(uint32_t tmem_d, uint32_t tmem_a, uint64_t b, uint32_t idesc,
+                                           uint32_t acc) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(tmem_d),
+      "r"(tmem_a), "l"(b), "r"(idesc), "r"(acc)
+      : "memory");
+}
+
 __device__ __forceinline__ void mma_commit(uint64_t* bar) {
   asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
                : "memory");
@@ -134,6 +151,19 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
   for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
 }
 
+// Same, without the wait: several loads can be in flight before one tcgen05.wait::ld.
+__device__ __forceinline__ void tmem_ld32_async(uint32_t taddr, uint32_t (&r)[32]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
+      "%15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%32];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]),
+        "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]), "=r"(r[16]),
+        "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]),
+        "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr)
+      : "memory");
+}
+
 __device__ __forceinline__ void tmem_st32(uint32_t taddr, const float (&v)[32]) {
   asm volatile(
       "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
@@ -148,6 +178,17 @@ __device__ __forceinline__ void tmem_st32(uint32_t taddr, const float (&v)[32]) 
       "r"(__float_as_uint(v[23])), "r"(__float_as_uint(v[24])), "r"(__float_as_uint(v[25])),
       "r"(__float_as_uint(v[26])), "r"(__float_as_uint(v[27])), "r"(__float_as_uint(v[28])),
       "r"(__float_as_uint(v[29])), "r"(__float_as_uint(v[30])), "r"(__float_as_uint(v[31]))
+      : "memory");
+}
+
+__device__ __forceinline__ void tmem_st32u(uint32_t taddr, const uint32_t (&v)[32]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
+      "%15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31, %32};" ::"r"(taddr),
+      "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7]), "r"(v[8]), "r"(v[9]),
+      "r"(v[10]), "r"(v[11]), "r"(v[12]), "r"(v[13]), "r"(v[14]), "r"(v[15]), "r"(v[16]), "r"(v[17]), "r"(v[18]),
+      "r"(v[19]), "r"(v[20]), "r"(v[21]), "r"(v[22]), "r"(v[23]), "r"(v[24]), "r"(v[25]), "r"(v[26]), "r"(v[27]),
+      "r"(v[28]), "r"(v[29]), "r"(v[30]), "r"(v[31])
       : "memory");
 }
 
@@ -172,10 +213,14 @@ __host__ __device__ constexpr uint32_t idesc_f16(uint32_t fmt, uint32_t b_mn_maj
 
 // Roles: warps 0-7 run the softmax: warp w covers TMEM lanes (rows) 32*(w%4).. and S/O columns
 // 64*(w/4).. of its row quadrant, so every row is shared by two warps that exchange their partial
-// max through shared memory; lane 0 of warp 8 is the producer that issues every TMA load and
-// every tcgen05.mma.
-constexpr int kSoftWarps = 8;
-constexpr int kThreadsTC = (kSoftWarps + 1) * 32;
+// max through shared memory; lane 0 of warp 8 issues every tcgen05.mma; lane 0 of warp 9 issues
+// every TMA load, waiting only on the "stage free" barriers the MMAs commit, so loads never hold
+// up MMA issue.
+constexpr int kWarpsPerQuad = 2;
+constexpr int kSoftWarps = 4 * kWarpsPerQuad;
+constexpr int kColsPerWarp = kKeys / kWarpsPerQuad;  // 64
+constexpr int kMmaWarp = kSoftWarps, kLoadWarp = kSoftWarps + 1;
+constexpr int kThreadsTC = (kSoftWarps + 2) * 32;
 
 struct Waiter {
   volatile int* abort;
@@ -198,15 +243,29 @@ __device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
   asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
 }
 
-// Barrier over the two softmax warps that share a row quadrant (named barrier 1 + quadrant).
-__device__ __forceinline__ void pair_sync(int quadrant) {
-  asm volatile("bar.sync %0, 64;" ::"r"(1 + quadrant) : "memory");
+// Barrier over the softmax warps that share a row quadrant (named barrier 1 + quadrant).
+__device__ __forceinline__ void quad_sync(int quadrant) {
+  asm volatile("bar.sync %0, %1;" ::"r"(1 + quadrant), "r"(kWarpsPerQuad * 32) : "memory");
 }
 
 __device__ __forceinline__ float ex2(float x) {
   float y;
   asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
   return y;
+}
+
+// 2^x on the FMA pipe, to take a quarter of the exponentials off the MUFU pipe (which otherwise
+// needs as many cycles per step as the tensor core): x = i + f with i = round(x) by the
+// 1.5 * 2^23 addition (FADDs only), 2^f on [-0.5, 0.5] from a cubic fitted here (iteratively
+// reweighted least squares on Chebyshev nodes, relative error) with max relative error 7.5e-5,
+// far below the rounding of P to bf16/fp16; 2^i is added to the exponent bits. Arguments below
+// -126 give 2^-126-scale values (probabilities that vanish next to the row maximum's 1).
+__device__ __forceinline__ float ex2_poly(float x) {
+  x = fmaxf(x, -126.f);
+  const float t = __fadd_rn(x, 12582912.f);
+  const float f = __fsub_rn(x, __fsub_rn(t, 12582912.f));
+  const float p = fmaf(fmaf(fmaf(0.055171654f, f, 0.24261113f), f, 0.69326097f), f, 0.99992806f);
+  return __int_as_float(__float_as_int(p) + (__float_as_int(t) << 23));
 }
 
 template <typename T>
@@ -220,22 +279,24 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
   unsigned char* sQ = smem;               // 2 blocks: d 0-63, d 64-127
   unsigned char* sK = smem + 2 * kBlock;  // 2 stages x 2 blocks
   unsigned char* sV = smem + 6 * kBlock;  // 2 stages x 2 blocks
-  unsigned char* sP = smem + 10 * kBlock; // 2 blocks: keys 0-63, 64-127
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + 12 * kBlock);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + 10 * kBlock);
   uint64_t* q_full = bars + 0;
-  uint64_t* k_full = bars + 1;   // [2]
-  uint64_t* v_full = bars + 3;   // [2]
-  uint64_t* s_full = bars + 5;   // [2]
-  uint64_t* s_free = bars + 7;   // [2]
-  uint64_t* p_full = bars + 9;
-  uint64_t* pv_done = bars + 10;
-  uint32_t* s_tmem = reinterpret_cast<uint32_t*>(bars + 11);
-  int* s_abort = reinterpret_cast<int*>(bars + 12);
+  uint64_t* k_full = bars + 1;   // [2] K stage loaded
+  uint64_t* v_full = bars + 3;   // [2] V stage loaded
+  uint64_t* s_full = bars + 5;   // [2] S buffer written by QK
+  uint64_t* s_free = bars + 7;   // [2] S buffer read by the softmax
+  uint64_t* p_full = bars + 9;   // [2] P buffer written by the softmax
+  uint64_t* pv_done = bars + 11; // [2] PV of P buffer b complete (buffer reusable, O stable)
+  uint64_t* k_free = bars + 13;  // [2] K stage read by its QK
+  uint64_t* v_free = bars + 15;  // [2] V stage read by its PV
+  constexpr int kNumBars = 17;
+  uint32_t* s_tmem = reinterpret_cast<uint32_t*>(bars + kNumBars);
+  int* s_abort = reinterpret_cast<int*>(bars + kNumBars + 1);
   __shared__ int s_wmax[4];
-  __shared__ float s_part[2][2][kRows];  // [step parity][column half][row]: partial max / final sum
+  __shared__ float s_part[2][kWarpsPerQuad][kRows];  // [step parity][column part][row]: max / final sum
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int quad = warp & 3, half = (warp >> 2) & 1;
+  const int quad = warp & 3, part = warp >> 2;
   const int h = blockIdx.x, g = h / G;
   const int tile = gridDim.y - 1 - blockIdx.y;  // latest rows (longest key ranges) start first
   const int r0 = tile * kRows;
@@ -245,7 +306,7 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
   const bool live = soft && row < R;
   long long p = live ? pos[row] : 0;
   if (p < 0 || p >= T_cache) {
-    if (live && half == 0 && err) atomicOr(err, 2u);
+    if (live && part == 0 && err) atomicOr(err, 2u);
     p = 0;
   }
   if (warp < 4) {
@@ -268,8 +329,14 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
     mbar_init(&s_full[1], 1);
     mbar_init(&s_free[0], kSoftWarps * 32);
     mbar_init(&s_free[1], kSoftWarps * 32);
-    mbar_init(p_full, kSoftWarps * 32);
-    mbar_init(pv_done, 1);
+    mbar_init(&p_full[0], kSoftWarps * 32);
+    mbar_init(&p_full[1], kSoftWarps * 32);
+    mbar_init(&pv_done[0], 1);
+    mbar_init(&pv_done[1], 1);
+    mbar_init(&k_free[0], 1);
+    mbar_init(&k_free[1], 1);
+    mbar_init(&v_free[0], 1);
+    mbar_init(&v_free[1], 1);
     *s_abort = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
@@ -280,15 +347,11 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
   const int nsteps = max(max(s_wmax[0], s_wmax[1]), max(s_wmax[2], s_wmax[3])) / kKeys + 1;
   const Waiter wait{s_abort};
 
-  if (!soft) {
-    // ------------------------------------------------------------------ producer (one lane)
+  if (warp == kLoadWarp) {
+    // ------------------------------------------------------------------ TMA loader (one lane)
+    // K and V have separate 2-stage rings; K(j+2) goes into its stage once QK(j) has read it and
+    // V(j+2) once PV(j) has, so copies run two steps ahead of the MMAs.
     if (lane == 0) {
-      constexpr uint32_t fmt = std::is_same<T, __nv_bfloat16>::value ? 1u : 0u;
-      constexpr uint32_t idesc_qk = idesc_f16(fmt, 0, kRows, kKeys);
-      constexpr uint32_t idesc_pv = idesc_f16(fmt, 1, kRows, kD);
-      const uint32_t aQ = smem_u32(sQ), aK = smem_u32(sK), aV = smem_u32(sV), aP = smem_u32(sP);
-      // K and V have separate 2-stage rings: K(j+2) is fetched as soon as QK(j) has read its
-      // stage, V(j+1) as soon as PV(j-1) has, so copies run two steps ahead of the MMAs.
       auto load_k = [&](int j) {
         const int s = j & 1;
         mbar_expect_tx(&k_full[s], 2 * kBlock);
@@ -301,23 +364,39 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
         tma_load_3d(sV + s * 2 * kBlock, &tm_v, &v_full[s], 0, j * kKeys, g);
         tma_load_3d(sV + s * 2 * kBlock + kBlock, &tm_v, &v_full[s], 64, j * kKeys, g);
       };
-      auto issue_pv = [&](int j) {
-        const uint32_t vbase = aV + (j & 1) * 2 * kBlock;
-#pragma unroll
-        for (int k = 0; k < kKeys / 16; ++k)
-          mma_f16(tmem + 256, sw128_desc(aP + (k >> 2) * kBlock + (k & 3) * 32, 16, 1024),
-                  sw128_desc(vbase + k * 16 * 128, kBlock, 1024), idesc_pv, (j > 0 || k > 0) ? 1u : 0u);
-        mma_commit(pv_done);
-      };
       mbar_expect_tx(q_full, 2 * kBlock);
       tma_load_3d(sQ, &tm_q, q_full, 0, h, r0);
       tma_load_3d(sQ + kBlock, &tm_q, q_full, 64, h, r0);
-      load_k(0);
-      load_v(0);
-      if (nsteps > 1) {
-        load_k(1);
-        load_v(1);
+      for (int j = 0; j < nsteps && j < 2; ++j) {
+        load_k(j);
+        load_v(j);
       }
+      for (int j = 0; j + 2 < nsteps; ++j) {
+        const int s = j & 1;
+        if (!wait(&k_free[s], (j >> 1) & 1)) break;
+        load_k(j + 2);
+        if (!wait(&v_free[s], (j >> 1) & 1)) break;
+        load_v(j + 2);
+      }
+    }
+  } else if (warp == kMmaWarp) {
+    // ------------------------------------------------------------------ MMA issuer (one lane)
+    if (lane == 0) {
+      constexpr uint32_t fmt = std::is_same<T, __nv_bfloat16>::value ? 1u : 0u;
+      constexpr uint32_t idesc_qk = idesc_f16(fmt, 0, kRows, kKeys);
+      constexpr uint32_t idesc_pv = idesc_f16(fmt, 1, kRows, kD);
+      const uint32_t aQ = smem_u32(sQ), aK = smem_u32(sK), aV = smem_u32(sV);
+      // PV(j): O += P_j V_j, P_j from TMEM (P buffer j%2: 64 columns of packed 16-bit pairs)
+      auto issue_pv = [&](int j) {
+        const int b = j & 1;
+        const uint32_t vbase = aV + b * 2 * kBlock;
+#pragma unroll
+        for (int k = 0; k < kKeys / 16; ++k)
+          mma_f16_ts(tmem + kTmemO, tmem + kTmemP + b * (kKeys / 2) + k * 8,
+                     sw128_desc(vbase + k * 16 * 128, kBlock, 1024), idesc_pv, (j > 0 || k > 0) ? 1u : 0u);
+        mma_commit(&pv_done[b]);
+        mma_commit(&v_free[b]);
+      };
       bool ok = true;
       for (int j = 0; j < nsteps && ok; ++j) {
         const int s = j & 1;
@@ -329,28 +408,21 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
 #pragma unroll
         for (int k = 0; k < kD / 16; ++k) {
           const uint32_t off = (k >> 2) * kBlock + (k & 3) * 32;
-          mma_f16(tmem + s * 128, sw128_desc(aQ + off, 16, 1024), sw128_desc(kbase + off, 16, 1024), idesc_qk,
+          mma_f16(tmem + s * kKeys, sw128_desc(aQ + off, 16, 1024), sw128_desc(kbase + off, 16, 1024), idesc_qk,
                   k > 0);
         }
         mma_commit(&s_full[s]);
+        mma_commit(&k_free[s]);
         if (j >= 1) {
-          ok = wait(p_full, (j - 1) & 1) && wait(&v_full[(j - 1) & 1], ((j - 1) >> 1) & 1);
+          const int b = (j - 1) & 1;
+          ok = wait(&p_full[b], ((j - 1) >> 1) & 1) && wait(&v_full[b], ((j - 1) >> 1) & 1);
           if (!ok) break;
           tc_fence_after();
           issue_pv(j - 1);
         }
-        if (j + 2 < nsteps) {
-          ok = wait(&s_full[s], (j >> 1) & 1);  // QK(j) has read K stage s
-          if (!ok) break;
-          load_k(j + 2);
-        }
-        if (j >= 1 && j + 1 < nsteps) {
-          ok = wait(pv_done, (j - 1) & 1);  // PV(j-1) has read V stage (j+1)&1
-          if (!ok) break;
-          load_v(j + 1);
-        }
       }
-      if (ok && wait(p_full, (nsteps - 1) & 1) && wait(&v_full[(nsteps - 1) & 1], ((nsteps - 1) >> 1) & 1)) {
+      const int b = (nsteps - 1) & 1;
+      if (ok && wait(&p_full[b], ((nsteps - 1) >> 1) & 1) && wait(&v_full[b], ((nsteps - 1) >> 1) & 1)) {
         tc_fence_after();
         issue_pv(nsteps - 1);
       }
@@ -358,31 +430,44 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
   } else {
     // ------------------------------------------------------------------ softmax
     const uint32_t lane_off = (uint32_t)(quad * 32) << 16;
-    const uint32_t col = half * 64;
-    const uint32_t tO = tmem + 256 + col;
-    float m = -INFINITY, l = 0.f;  // l: this half's partial row sum
+    const uint32_t col = part * kColsPerWarp;
+    const uint32_t tO = tmem + kTmemO + col;
+    float m = -INFINITY, l = 0.f;  // l: this part's share of the row sum
     bool ok = true;
     for (int j = 0; j < nsteps; ++j) {
       const int s = j & 1;
-      const uint32_t tS = tmem + s * 128 + col;
       ok = __all_sync(0xffffffffu, wait(&s_full[s], (j >> 1) & 1));
       if (!ok) break;
       tc_fence_after();
-      float v[64];
-      tmem_ld32(tS + lane_off, *reinterpret_cast<float(*)[32]>(v));
-      tmem_ld32(tS + lane_off + 32, *reinterpret_cast<float(*)[32]>(v + 32));
-      const long long key0 = (long long)j * kKeys + col;
-      if (__any_sync(0xffffffffu, key0 + 63 > p)) {
+      float v[kColsPerWarp];
+      {
+        uint32_t r[kColsPerWarp / 32][32];
 #pragma unroll
-        for (int i = 0; i < 64; ++i)
+        for (int c = 0; c < kColsPerWarp / 32; ++c)
+          tmem_ld32_async(tmem + s * kKeys + col + c * 32 + lane_off, r[c]);
+        asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+        for (int c = 0; c < kColsPerWarp / 32; ++c)
+#pragma unroll
+          for (int i = 0; i < 32; ++i) v[c * 32 + i] = __uint_as_float(r[c][i]);
+      }
+      // S buffer s is in registers: QK(j+2) may overwrite it
+      tc_fence_before();
+      mbar_arrive(&s_free[s]);
+      const long long key0 = (long long)j * kKeys + col;
+      if (__any_sync(0xffffffffu, key0 + kColsPerWarp - 1 > p)) {
+#pragma unroll
+        for (int i = 0; i < kColsPerWarp; ++i)
           if (key0 + i > p) v[i] = -INFINITY;
       }
       float tmax = v[0];
 #pragma unroll
-      for (int i = 1; i < 64; ++i) tmax = fmaxf(tmax, v[i]);
-      s_part[s][half][trow] = tmax * scale_log2;
-      pair_sync(quad);
-      const float m_new = fmaxf(m, fmaxf(tmax * scale_log2, s_part[s][half ^ 1][trow]));
+      for (int i = 1; i < kColsPerWarp; ++i) tmax = fmaxf(tmax, v[i]);
+      s_part[s][part][trow] = tmax * scale_log2;
+      quad_sync(quad);
+      float m_new = m;
+#pragma unroll
+      for (int q = 0; q < kWarpsPerQuad; ++q) m_new = fmaxf(m_new, s_part[s][q][trow]);
       const bool rescale = j > 0 && m_new > m + 8.f;
       float alpha = 1.f;
       if (j == 0 || rescale) {
@@ -390,52 +475,55 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
         l *= alpha;
         m = m_new;
       }
-      if (j > 0) {  // PV(j-1) done: P may be overwritten and O is stable
-        ok = __all_sync(0xffffffffu, wait(pv_done, (j - 1) & 1));
+      // P (this part's 64 keys, packed in pairs) in registers; one in four exponentials on the FMA pipe
+      uint32_t pk[kColsPerWarp / 2];
+#pragma unroll
+      for (int i = 0; i < kColsPerWarp; i += 2) {
+        const float p0 = ex2(fmaf(v[i], scale_log2, -m));
+        const float x1 = fmaf(v[i + 1], scale_log2, -m);
+        const float p1 = ((i >> 1) & 1) ? ex2_poly(x1) : ex2(x1);
+        l += p0 + p1;
+        pk[i / 2] = pack2<T>(p0, p1);
+      }
+      // P buffer s was last read by PV(j-2)
+      if (j >= 2) {
+        ok = __all_sync(0xffffffffu, wait(&pv_done[s], ((j - 2) >> 1) & 1));
+        if (!ok) break;
+      }
+      // O must be stable (PV(j-1) complete) to rescale it; tcgen05.ld/st are warp-collective, so
+      // the warp rescales together, other lanes by 1
+      if (__any_sync(0xffffffffu, rescale)) {
+        ok = __all_sync(0xffffffffu, wait(&pv_done[s ^ 1], ((j - 1) >> 1) & 1));
         if (!ok) break;
         tc_fence_after();
-      }
-      // tcgen05.ld/st are warp-collective: the warp rescales together, other lanes by 1
-      if (__any_sync(0xffffffffu, rescale)) {
 #pragma unroll 1
-        for (int c = 0; c < 2; ++c) {
+        for (int c = 0; c < kColsPerWarp / 32; ++c) {
           float o[32];
           tmem_ld32(tO + lane_off + c * 32, o);
 #pragma unroll
           for (int i = 0; i < 32; ++i) o[i] *= alpha;
           tmem_st32(tO + lane_off + c * 32, o);
         }
-        asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+      } else if (j >= 2) {
+        tc_fence_after();
       }
-      // P row half -> shared memory block `half` (keys 64*half..), K-major 128B-swizzled:
-      // 16-byte chunk q of an 8-row atom row goes to q ^ (row % 8)
-      unsigned char* blk = sP + half * kBlock + (trow >> 3) * 1024 + (trow & 7) * 128;
-#pragma unroll
-      for (int q = 0; q < 8; ++q) {
-        uint32_t pk[4];
-#pragma unroll
-        for (int i = 0; i < 8; i += 2) {
-          const float p0 = ex2(fmaf(v[q * 8 + i], scale_log2, -m));
-          const float p1 = ex2(fmaf(v[q * 8 + i + 1], scale_log2, -m));
-          l += p0 + p1;
-          pk[i / 2] = pack2<T>(p0, p1);
-        }
-        *reinterpret_cast<uint4*>(blk + ((q ^ (trow & 7)) << 4)) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
-      }
+      tmem_st32u(tmem + kTmemP + s * (kKeys / 2) + part * (kColsPerWarp / 2) + lane_off, pk);
+      asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
       tc_fence_before();
-      mbar_arrive(&s_free[s]);  // S buffer s fully read
-      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-      mbar_arrive(p_full);
+      mbar_arrive(&p_full[s]);
     }
-    if (ok) ok = __all_sync(0xffffffffu, wait(pv_done, (nsteps - 1) & 1));
+    if (ok) ok = __all_sync(0xffffffffu, wait(&pv_done[(nsteps - 1) & 1], ((nsteps - 1) >> 1) & 1));
     if (ok) {
       tc_fence_after();
-      s_part[0][half][trow] = l;
-      pair_sync(quad);
-      const float inv = 1.f / (l + s_part[0][half ^ 1][trow]);
+      s_part[0][part][trow] = l;
+      quad_sync(quad);
+      float lsum = 0.f;
+#pragma unroll
+      for (int q = 0; q < kWarpsPerQuad; ++q) lsum += s_part[0][q][trow];
+      const float inv = 1.f / lsum;
       T* orow = out + ((long long)row * Hq + h) * kD + col;
 #pragma unroll 1
-      for (int c = 0; c < 2; ++c) {
+      for (int c = 0; c < kColsPerWarp / 32; ++c) {
         float o[32];
         tmem_ld32(tO + lane_off + c * 32, o);
         if (live) {
@@ -453,14 +541,11 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
   __syncthreads();
   if (*s_abort && tid == 0) {
     if (err) atomicOr(err, 4u);
-    // let copies and MMAs already issued land before the CTA's resources go away
-    for (int b = 0; b < 2; ++b) {
-      mbar_wait(pv_done, b);
-      mbar_wait(&k_full[0], b);
-      mbar_wait(&k_full[1], b);
-      mbar_wait(&v_full[0], b);
-      mbar_wait(&v_full[1], b);
-    }
+    // let copies and MMAs already issued land before the CTA's resources go away: each barrier
+    // an async unit arrives on gets a short bounded wait on both parities
+    for (int b = 0; b < 2; ++b)
+      for (int i = 0; i < kNumBars; ++i)
+        if (i != 7 && i != 8 && i != 9 && i != 10) mbar_wait(bars + i, b, kAbortWaitNs);
   }
   __syncthreads();
   if (warp == 0) {
