@@ -17,6 +17,12 @@ tread/blend.py:22-39). Algorithmic bytes per step = read K+V + write K+V = 939.5
 
 Multi-GPU: every rank assembles its own requests from its own pool (weak scaling, no
 collective on the data path).
+
+TTFT legs (objects on the same line): `ttft` (1 GPU) is the configs[2] 7B request through the
+single-GPU engine, graphed and eager, at ratios 0 / 0.2 / 0.5 / 1.0. `ttft_tp` is the model split
+over the N GPUs by KV head (tread_b200.tp, NCCL all-reduce after o_proj and down_proj): the
+configs[3] 32B request at tp = N (also at N = 1, where it fits one GPU), and at N > 1 the 7B
+request at tp = min(N, 4) (4 KV heads; replicas beyond that).
 """
 import argparse
 import json
@@ -56,6 +62,8 @@ def parse():
     ap.add_argument("--only", choices=["attention", "selector"], default=None,
                     help="run one kernel microbench alone (for profiler captures) and print its timing")
     ap.add_argument("--ttft-reps", type=int, default=5, help="timed warm requests per recompute ratio")
+    ap.add_argument("--no-tp", action="store_true",
+                    help="skip the KV-head tensor-parallel TTFT legs (configs[2] 7B, configs[3] 32B)")
     return ap.parse_args()
 
 
@@ -299,7 +307,15 @@ def run_gpu(args):
     selector = run_selector(args, dev, out_k, out_v, world)
     del plans, pool_k, pool_v, out_k, out_v
     torch.cuda.empty_cache()
-    ttft = None if args.no_ttft else run_ttft(args, dev, world)
+    # one GPU: the 7B request through the single-GPU engine (graphed and eager); N GPUs: the same
+    # request tensor-parallel by KV head (below) instead
+    ttft = None if args.no_ttft or world > 1 else run_ttft(args, dev, world)
+    ttft_tp = None
+    if not args.no_tp:
+        ttft_tp = {}
+        if world > 1 and not args.no_ttft:
+            ttft_tp["qwen2.5-7b"] = run_ttft_tp(args, dev, world, rank, "qwen2.5-7b", 256, 16, 496, 64)
+        ttft_tp["qwen2.5-32b"] = run_ttft_tp(args, dev, world, rank, "qwen2.5-32b", 512, 32, 500, 128)
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
@@ -324,6 +340,7 @@ def run_gpu(args):
             "e2e": e2e,
             "selector": selector,
             "ttft": ttft,
+            "ttft_tp": ttft_tp,
             "gpu_launches": args.steps,
             "clocks": clk,
         }
@@ -422,6 +439,79 @@ def run_ttft(args, dev, world):
     out["full_prefill_p50_ms"] = round(statistics.median(full) * 1e3, 2)
     del model
     torch.cuda.empty_cache()
+    return out
+
+
+def run_ttft_tp(args, dev, world, rank, arch, prefix_len, ndocs, doc_len, q_len):
+    """TTFT of one reordered-RAG request with the model split over the GPUs by KV head
+    (tread_b200.tp): BASELINE configs[3] (32B: 512 + 32 x 500 + 128 tokens, 20% recompute) and
+    the configs[2] 7B request at N GPUs. tp = the largest divisor of the KV-head count that also
+    divides N; with more GPUs than that, the groups are independent replicas serving the same
+    request. Weights are seeded random init drawn layer by layer on the device (the same model at
+    every tp). Pass 1 (cold) fills each rank's store with its head slice of every block; each
+    timed request is a fresh seeded permutation of the docs, host ids in and first token out on
+    the host, timed per rank by wall clock; reported per rep as the max over ranks, p50 over
+    --ttft-reps. KL is against a full prefill on the same sharded layer math."""
+    import torch.distributed as dist
+
+    from tread_b200 import BlockStore, Engine, prefill_full
+    from tread_b200.configs import qwen2_config, random_tokens
+    from tread_b200.tp import TPQwen2Rows
+
+    cfg = qwen2_config(arch)
+    hkv = cfg.num_key_value_heads
+    tp = max(d for d in range(1, min(world, hkv) + 1) if hkv % d == 0 and world % d == 0)
+    group = None
+    if world > 1 and tp < world:
+        for g0 in range(0, world, tp):  # every rank creates every group
+            grp = dist.new_group(list(range(g0, g0 + tp)))
+            if g0 <= rank < g0 + tp:
+                group = grp
+    barrier(world)
+    t_init = time.perf_counter()
+    net = TPQwen2Rows.random(cfg, group=group, seed=args.seed, dtype=torch.bfloat16, device=dev)
+    torch.cuda.synchronize(dev)
+    init_s = max_over_ranks(time.perf_counter() - t_init, world, dev)
+    V = cfg.vocab_size
+    g = torch.Generator().manual_seed(args.seed + 11)
+    prefix = random_tokens(prefix_len, V, g)
+    docs = [random_tokens(doc_len, V, g) for _ in range(ndocs)]
+    query = random_tokens(q_len, V, g)
+    eng = Engine(net, BlockStore(1 << 40))
+    eng.prefill(prefix, docs, query)  # pass 1: cold, fills every rank's store
+    pg = torch.Generator().manual_seed(args.seed + 13)
+    res = {}
+    for ratio in (0.0, 0.2):
+        times, stages = [], []
+        for rep in range(2 + args.ttft_reps):
+            order = [docs[i] for i in torch.randperm(ndocs, generator=pg).tolist()]
+            barrier(world)
+            torch.cuda.synchronize(dev)
+            t0 = time.perf_counter()
+            logits, cache, st = eng.prefill(prefix, order, query, ratio=ratio)
+            tok = int(logits.argmax().item())
+            t1 = time.perf_counter()
+            del cache
+            if rep >= 2:
+                times.append(max_over_ranks(t1 - t0, world, dev))
+                stages.append(st.t)
+        r = {"p50_ms": round(statistics.median(times) * 1e3, 2), "min_ms": round(min(times) * 1e3, 2),
+             "stages_p50_ms": {k: round(statistics.median(s_[k] for s_ in stages) * 1e3, 2) for k in stages[0]},
+             "recompute_eff": round(st.recompute_eff, 4), "hits": st.hits, "misses": st.misses}
+        if ratio == 0.2:
+            ref, _, _ = prefill_full(net, prefix, order, query)
+            r["kl_vs_full_prefill"] = round(kl_div(logits, ref), 5)
+            r["top1_eq_full"] = tok == int(ref.argmax())
+        res[str(ratio)] = r
+    out = {"workload": f"{arch} reordered RAG, {prefix_len} + {ndocs}x{doc_len} + {q_len} tokens, bf16, "
+                       f"KV-head tensor parallel",
+           "tp": tp, "replicas": world // tp, "init_s": round(init_s, 1),
+           "per_rank_weights_gb": round(sum(t.numel() * t.element_size() for l in net.layers for t in l.values()
+                                            if torch.is_tensor(t)) / 1e9, 2),
+           "ratios": res, "p50_ms_20pct": res["0.2"]["p50_ms"]}
+    del eng, net
+    torch.cuda.empty_cache()
+    barrier(world)
     return out
 
 

@@ -105,6 +105,31 @@ int tread_deviation_topk(const void* k1, const void* v1, int64_t fresh_stride_to
                          tread_stream_t stream);
 
 /*
+ * The same selector split for KV-head tensor parallelism (the reference is single-GPU; this
+ * is tread/blend.py:129,160,165 with the head sum spread over ranks). Each rank holds the
+ * contiguous head slice [r*Hkv, (r+1)*Hkv) of the layer-1 rows and cache:
+ *
+ * tread_deviation_head_norms writes norms_out, device fp32 [2][Hkv][n]:
+ *   norms_out[0][h][t] = ||k1[h,t] - K1[h,pos_t]||_2,  norms_out[1][h][t] = same for v1/V1,
+ * each computed exactly as inside tread_deviation_topk (same element/lane/butterfly order).
+ * Arguments as for tread_deviation_topk (Hkv <= 32); workspace word 1 is the same sticky
+ * out-of-range flag (those norms are NaN).
+ *
+ * tread_select_head_norms takes the all-gathered norms of every head, device fp32 [2][H][n]
+ * in global head order, forms dev[t] = (((nk_0 + nk_1) + ...) + ((nv_0 + nv_1) + ...)) -- the
+ * fused kernel's order, so the result equals a single-GPU tread_deviation_topk bit for bit --
+ * and selects exactly as tread_deviation_topk does (dev_out, sel_idx, sel_pos, workspace alike).
+ */
+int tread_deviation_head_norms(const void* k1, const void* v1, int64_t fresh_stride_tok,
+                               int64_t fresh_stride_head, const void* K1, const void* V1,
+                               int64_t cache_stride_tok, int64_t cache_stride_head, int64_t T_cache,
+                               const int64_t* cand_pos, int n, int Hkv, int D, int dtype,
+                               float* norms_out, void* workspace, tread_stream_t stream);
+int tread_select_head_norms(const float* norms, int n, int Hkv, int budget, const int64_t* cand_pos,
+                            float* dev_out, int64_t* sel_idx, int64_t* sel_pos, void* workspace,
+                            tread_stream_t stream);
+
+/*
  * Allocation-free variant of tread_deviation_topk. It has no counterpart in the reference; it
  * exists for callers that cannot provide device scratch: serving loops whose device memory is
  * owned by a pooling allocator reserved at start-up, loops that avoid cudaMalloc because it can

@@ -154,6 +154,33 @@ def deviation(k1, v1, K1, V1, cand_pos):
     return dev
 
 
+def head_norms(k1, v1, K1, V1, cand_pos):
+    """Per-head terms of tread/blend.py:129 in the kernel's fixed order: [2, H, n] fp32 with
+    [0, h, t] = ||k1[h,t] - K1[h,pos_t]|| and [1, h, t] the same for V. Each term is the
+    single-head `deviation` with the other side's rows set equal (so that side adds an exact 0)."""
+    k1, v1, K1, V1 = (np.ascontiguousarray(a) for a in (k1, v1, K1, V1))
+    H, n, D = k1.shape
+    zf = np.zeros((1, n, D), k1.dtype)
+    zc = np.zeros((1, K1.shape[1], D), K1.dtype)
+    out = np.empty((2, H, n), np.float32)
+    for h in range(H):
+        out[0, h] = deviation(k1[h:h + 1], zf, K1[h:h + 1], zc, cand_pos)
+        out[1, h] = deviation(zf, v1[h:h + 1], zc, V1[h:h + 1], cand_pos)
+    return out
+
+
+def dev_from_head_norms(norms):
+    """dev[t] = (((nk_0 + nk_1) + ...) + ((nv_0 + nv_1) + ...)) in fp32, the fused kernel's order
+    (tread/blend.py:129 sums K and V norms over heads)."""
+    a = np.zeros(norms.shape[2], np.float32)
+    b = np.zeros(norms.shape[2], np.float32)
+    for h in range(norms.shape[1]):
+        a = (a + norms[0, h]).astype(np.float32)
+    for h in range(norms.shape[1]):
+        b = (b + norms[1, h]).astype(np.float32)
+    return (a + b).astype(np.float32)
+
+
 def order_key(dev):
     """Order-preserving uint32 image of fp32 values (NaN above +inf, as torch.topk ranks it)."""
     u = np.ascontiguousarray(dev, dtype=np.float32).view(np.uint32)

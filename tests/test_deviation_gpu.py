@@ -92,3 +92,55 @@ def test_out_of_range_position_sets_flag(cuda):
     torch.cuda.synchronize()
     assert ws[1].item() == 1 and torch.isnan(dev[5])
     assert sel.tolist() == [5, 0, 1] or sorted(sel.tolist()) == [0, 1, 5]
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+@pytest.mark.parametrize("world", [1, 2, 4])
+def test_split_selector_matches_fused(cuda, dtype, world):
+    """KV-head tensor-parallel selector: per-head norms of each rank's head slice (bit-exact vs
+    the oracle), concatenated in rank order, then the fixed-order head sum + top-k: dev and
+    selection equal the single-GPU fused kernel's bit for bit (ranks emulated on one GPU)."""
+    g = torch.Generator().manual_seed(7 + world)
+    H, n, T, D = 4, 3001, 4100, 128
+    k1 = torch.randn(H, n, D, generator=g).to(dtype)
+    v1 = torch.randn(H, n, D, generator=g).to(dtype)
+    K1 = torch.randn(H, T, D, generator=g).to(dtype)
+    V1 = torch.randn(H, T, D, generator=g).to(dtype)
+    pos = torch.randperm(T, generator=g)[:n].sort().values
+    # plant exact ties across the cut: duplicate some candidates' rows onto others
+    K1[:, pos[100:140]] = K1[:, pos[0:40]]
+    V1[:, pos[100:140]] = V1[:, pos[0:40]]
+    k1[:, 100:140] = k1[:, 0:40]
+    v1[:, 100:140] = v1[:, 0:40]
+    d = [x.to(cuda) for x in (k1, v1, K1, V1, pos)]
+    budget = orc.budget_for(0.2, n)
+    dev_f, sel_f, pos_f = kernels.deviation_topk(*d, budget)
+    parts = []
+    per = H // world
+    for r in range(world):
+        s = slice(r * per, (r + 1) * per)
+        parts.append(kernels.deviation_head_norms(d[0][s], d[1][s], d[2][s], d[3][s], d[4]))
+    norms = torch.cat(parts, dim=1)
+    ref_norms = orc.head_norms(host(k1), host(v1), host(K1), host(V1), pos.numpy())
+    np.testing.assert_array_equal(norms.cpu().numpy(), ref_norms)
+    dev_s, sel_s, pos_s = kernels.select_head_norms(norms, d[4], budget)
+    np.testing.assert_array_equal(dev_s.cpu().numpy(), dev_f.cpu().numpy())
+    np.testing.assert_array_equal(dev_s.cpu().numpy(), orc.dev_from_head_norms(ref_norms))
+    np.testing.assert_array_equal(sel_s.cpu().numpy(), sel_f.cpu().numpy())
+    np.testing.assert_array_equal(pos_s.cpu().numpy(), pos_f.cpu().numpy())
+
+
+def test_split_selector_edge_cases(cuda):
+    """n = 0, budget 0 and budget n through the split selector."""
+    H, D = 2, 64
+    e = torch.empty(H, 0, D, device=cuda)
+    K = torch.randn(H, 16, D, device=cuda)
+    z = torch.empty(0, dtype=torch.int64, device=cuda)
+    assert kernels.deviation_head_norms(e, e, K, K, z).shape == (2, H, 0)
+    k1 = torch.randn(H, 9, D, device=cuda)
+    pos = torch.arange(9, device=cuda)
+    norms = kernels.deviation_head_norms(k1, k1, K, K, pos)
+    dev, sel, _ = kernels.select_head_norms(norms, pos, 0)
+    assert sel.numel() == 0 and dev.shape == (9,)
+    _, sel, p = kernels.select_head_norms(norms, pos, 9)
+    np.testing.assert_array_equal(sel.cpu().numpy(), np.arange(9))

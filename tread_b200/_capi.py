@@ -41,6 +41,14 @@ SIGNATURES = {
         [P, P, I64, I64, P, P, I64, I64, I64, P, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int,
          ctypes.c_int, P, P, P],
     ),
+    "tread_deviation_head_norms": (
+        ctypes.c_int,
+        [P, P, I64, I64, P, P, I64, I64, I64, P, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int, P, P, P],
+    ),
+    "tread_select_head_norms": (
+        ctypes.c_int,
+        [P, ctypes.c_int, ctypes.c_int, ctypes.c_int, P, P, P, P, P, P],
+    ),
     "tread_rope_rows": (
         ctypes.c_int,
         [P, I64, P, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int, P, P, P, I64, I64, ctypes.c_int, PF32,

@@ -16,7 +16,11 @@ from tread_b200.qwen2 import Qwen2Rows
 
 
 def rows_of(model) -> Qwen2Rows:
-    """The layer math bound to `model` (built once, cached on the model object)."""
+    """The layer math bound to `model` (built once, cached on the model object). A rows object
+    (e.g. a KV-head tensor-parallel shard, tread_b200.tp) stands for its model and is returned
+    as is."""
+    if isinstance(model, Qwen2Rows):
+        return model
     r = getattr(model, "_tread_b200_rows", None)
     if r is None:
         r = Qwen2Rows(model)
@@ -93,7 +97,7 @@ def _deviation_pass(net, ctx_ids, K, V, all_c, inplace, extra, budget):
     v1 = torch.empty_like(k1)
     kernels.rope_rows(qkv1, all_c, net.Hq, net.Hkv, net.D, None, k1, v1, net.inv_freq, net.attn_scaling, net.err,
                       kv_by_row=True)
-    dev, sel_idx, S = kernels.deviation_topk(k1, v1, K[1], V[1], all_c, budget)
+    dev, sel_idx, S = net.deviation_select(k1, v1, K[1], V[1], all_c, budget)
     return dev, sel_idx, S, hc, K0, V0, (h[n:] if extra is not None else None)
 
 

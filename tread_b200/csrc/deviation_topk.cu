@@ -16,6 +16,8 @@
 //   fl(p + fl(d*d)) in element order, d = fl(fresh - cached); lanes then combine by an xor
 //   butterfly with offsets 16, 8, 4, 2, 1; norm = sqrt (IEEE); per token
 //   a = (((n_k0 + n_k1) + n_k2) + ...), b likewise over V heads, dev = a + b.
+#include <algorithm>
+
 #include "common.cuh"
 
 namespace tread {
@@ -302,6 +304,155 @@ extern "C" int tread_deviation_topk(const void* k1, const void* v1, int64_t fres
                                cache_stride_head, T_cache, cand_pos, n, Hkv, budget, dev_out, sel_idx, sel_pos, ws,
                                st);
   }
+}
+
+// ---- tensor-parallel split: per-head norms on each rank, selection on the gathered norms ------------
+//
+// Under KV-head tensor parallelism each rank holds a contiguous slice of the KV heads. A rank
+// writes the per-head norms of its slice (the phase-1 values before the head sums); after an
+// all-gather every rank holds all heads' norms, sums them in global head order exactly as the
+// fused kernel does (a = ((n_k0 + n_k1) + ...), b likewise, dev = a + b) and runs the same
+// selection, so every rank selects the same tokens and a single-rank run selects the same set.
+
+namespace tread {
+namespace {
+
+template <typename T, int E>
+__global__ void __launch_bounds__(kThreads)
+    head_norms_kernel(const T* __restrict__ k1, const T* __restrict__ v1, long long f_st, long long f_sh,
+                      const T* __restrict__ K1, const T* __restrict__ V1, long long c_st, long long c_sh,
+                      long long T_cache, const int64_t* __restrict__ cand_pos, int n, int H,
+                      float* __restrict__ norms, unsigned* __restrict__ workspace) {
+  const int lane = threadIdx.x & 31;
+  const int t = blockIdx.x * kWarps + (threadIdx.x >> 5);
+  if (t >= n) return;
+  const long long pos = cand_pos[t];
+  if (pos < 0 || pos >= T_cache) {
+    if (lane == 0) atomicOr(workspace + 1, 1u);
+    if (lane < H) {
+      norms[(long long)lane * n + t] = __int_as_float(0x7fc00000);
+      norms[(long long)(H + lane) * n + t] = __int_as_float(0x7fc00000);
+    }
+    return;
+  }
+#pragma unroll 1
+  for (int h = 0; h < H; ++h) {
+    float fk[E], ck[E], fv[E], cv[E];
+    const long long fo = (long long)t * f_st + (long long)h * f_sh + lane * E;
+    const long long co = pos * c_st + (long long)h * c_sh + lane * E;
+    load_row<T, E>(k1 + fo, fk);
+    load_row<T, E>(K1 + co, ck);
+    load_row<T, E>(v1 + fo, fv);
+    load_row<T, E>(V1 + co, cv);
+    const float nk = row_norm<E>(fk, ck);
+    const float nv = row_norm<E>(fv, cv);
+    if (lane == 0) {
+      norms[(long long)h * n + t] = nk;
+      norms[(long long)(H + h) * n + t] = nv;
+    }
+  }
+}
+
+// norms: [2][H][n] fp32 (K heads, then V heads, in global head order).
+__global__ void __launch_bounds__(kThreads)
+    select_head_norms_kernel(const float* __restrict__ norms, int n, int H, int budget,
+                             const int64_t* __restrict__ cand_pos, float* __restrict__ dev_out,
+                             int64_t* __restrict__ sel_idx, int64_t* __restrict__ sel_pos,
+                             unsigned* __restrict__ workspace) {
+  for (int t = blockIdx.x * kThreads + threadIdx.x; t < n; t += gridDim.x * kThreads) {
+    float a = 0.f, b = 0.f;
+    for (int h = 0; h < H; ++h) a = __fadd_rn(a, norms[(long long)h * n + t]);
+    for (int h = 0; h < H; ++h) b = __fadd_rn(b, norms[(long long)(H + h) * n + t]);
+    dev_out[t] = __fadd_rn(a, b);
+  }
+  if (budget <= 0) return;
+  __shared__ bool s_last;
+  __threadfence();
+  __syncthreads();
+  if (threadIdx.x == 0) s_last = atomicAdd(workspace, 1u) == gridDim.x - 1;
+  __syncthreads();
+  if (!s_last) return;
+  __threadfence();
+  select_topk(dev_out, n, budget, cand_pos, sel_idx, sel_pos);
+  if (threadIdx.x == 0) workspace[0] = 0u;
+}
+
+template <typename T>
+int launch_head_norms(int D, const void* k1, const void* v1, long long f_st, long long f_sh, const void* K1,
+                      const void* V1, long long c_st, long long c_sh, long long T_cache, const int64_t* cand_pos,
+                      int n, int H, float* norms, unsigned* ws, cudaStream_t st) {
+  const int grid = (n + kWarps - 1) / kWarps;
+#define TREAD_HN(E_)                                                                                              \
+  head_norms_kernel<T, E_><<<grid, kThreads, 0, st>>>(static_cast<const T*>(k1), static_cast<const T*>(v1), f_st, \
+                                                      f_sh, static_cast<const T*>(K1), static_cast<const T*>(V1),  \
+                                                      c_st, c_sh, T_cache, cand_pos, n, H, norms, ws)
+  switch (D) {
+    case 64: TREAD_HN(2); break;
+    case 128: TREAD_HN(4); break;
+    default: TREAD_HN(8); break;
+  }
+#undef TREAD_HN
+  TREAD_CHECK_LAUNCH("head_norms_kernel");
+  return TREAD_OK;
+}
+
+}  // namespace
+}  // namespace tread
+
+extern "C" int tread_deviation_head_norms(const void* k1, const void* v1, int64_t fresh_stride_tok,
+                                          int64_t fresh_stride_head, const void* K1, const void* V1,
+                                          int64_t cache_stride_tok, int64_t cache_stride_head, int64_t T_cache,
+                                          const int64_t* cand_pos, int n, int Hkv, int D, int dtype,
+                                          float* norms_out, void* workspace, tread_stream_t stream) {
+  using namespace tread;
+  TREAD_CHECK_ARG(n >= 0, "deviation_head_norms: n < 0");
+  if (n == 0) return TREAD_OK;
+  TREAD_CHECK_ARG(k1 && v1 && K1 && V1 && cand_pos && norms_out && workspace, "deviation_head_norms: null pointer");
+  TREAD_CHECK_ARG(Hkv > 0 && Hkv <= 32 && (D == 64 || D == 128 || D == 256),
+                  "deviation_head_norms: need 0 < Hkv <= 32 and D in {64,128,256}");
+  const size_t es = dtype_size(dtype);
+  TREAD_CHECK_ARG(es != 0, "deviation_head_norms: unknown dtype %d", dtype);
+  const int E = D / 32;
+  const size_t vec_bytes = E * es;
+  auto al = [&](const void* p) { return (reinterpret_cast<uintptr_t>(p) % vec_bytes) == 0; };
+  TREAD_CHECK_ARG(al(k1) && al(v1) && al(K1) && al(V1), "deviation_head_norms: row pointers not %zu-byte aligned",
+                  vec_bytes);
+  TREAD_CHECK_ARG(fresh_stride_tok % E == 0 && fresh_stride_head % E == 0 && cache_stride_tok % E == 0 &&
+                      cache_stride_head % E == 0,
+                  "deviation_head_norms: strides must be multiples of D/32");
+  TREAD_CHECK_ARG(T_cache > 0, "deviation_head_norms: T_cache must be > 0");
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  unsigned* ws = static_cast<unsigned*>(workspace);
+  switch (dtype) {
+    case TREAD_BF16:
+      return launch_head_norms<__nv_bfloat16>(D, k1, v1, fresh_stride_tok, fresh_stride_head, K1, V1,
+                                              cache_stride_tok, cache_stride_head, T_cache, cand_pos, n, Hkv,
+                                              norms_out, ws, st);
+    case TREAD_F16:
+      return launch_head_norms<__half>(D, k1, v1, fresh_stride_tok, fresh_stride_head, K1, V1, cache_stride_tok,
+                                       cache_stride_head, T_cache, cand_pos, n, Hkv, norms_out, ws, st);
+    default:
+      return launch_head_norms<float>(D, k1, v1, fresh_stride_tok, fresh_stride_head, K1, V1, cache_stride_tok,
+                                      cache_stride_head, T_cache, cand_pos, n, Hkv, norms_out, ws, st);
+  }
+}
+
+extern "C" int tread_select_head_norms(const float* norms, int n, int Hkv, int budget, const int64_t* cand_pos,
+                                       float* dev_out, int64_t* sel_idx, int64_t* sel_pos, void* workspace,
+                                       tread_stream_t stream) {
+  using namespace tread;
+  TREAD_CHECK_ARG(n >= 0 && budget >= 0 && budget <= n, "select_head_norms: need 0 <= budget (%d) <= n (%d)",
+                  budget, n);
+  if (n == 0) return TREAD_OK;
+  TREAD_CHECK_ARG(norms && dev_out && workspace && Hkv > 0, "select_head_norms: null pointer or Hkv <= 0");
+  TREAD_CHECK_ARG(budget == 0 || (sel_idx && (cand_pos || !sel_pos)), "select_head_norms: sel_idx/cand_pos null");
+  TREAD_CHECK_ARG((reinterpret_cast<uintptr_t>(workspace) & 15u) == 0, "select_head_norms: workspace not aligned");
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  const int grid = std::min((n + kThreads - 1) / kThreads, 148 * 4);
+  select_head_norms_kernel<<<grid, kThreads, 0, st>>>(norms, n, Hkv, budget, cand_pos, dev_out, sel_idx, sel_pos,
+                                                      static_cast<unsigned*>(workspace));
+  TREAD_CHECK_LAUNCH("select_head_norms_kernel");
+  return TREAD_OK;
 }
 
 // ---- allocation-free variant -------------------------------------------------------------------

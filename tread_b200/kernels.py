@@ -208,6 +208,73 @@ def deviation_topk(k1, v1, K1, V1, cand_pos, budget, dev_out=None, sel_idx=None,
     return dev_out, sel_idx, sel_pos
 
 
+def deviation_head_norms(k1, v1, K1, V1, cand_pos, norms_out=None, ws=None, stream=None):
+    """Per-head layer-1 deviation norms of this rank's KV-head slice: fp32 [2, H, n] (K heads,
+    then V heads), each norm computed exactly as inside `deviation_topk`."""
+    k1, f_st, f_sh = _rows_view(k1, "k1")
+    v1, f_st2, f_sh2 = _rows_view(v1, "v1")
+    K1, c_st, c_sh = _rows_view(K1, "K1")
+    V1, c_st2, c_sh2 = _rows_view(V1, "V1")
+    if (f_st, f_sh) != (f_st2, f_sh2) or (c_st, c_sh) != (c_st2, c_sh2):
+        raise ValueError("k1/v1 (and K1/V1) must share strides")
+    H, n, D = k1.shape
+    if v1.shape != k1.shape or K1.shape[0] != H or K1.shape[2] != D or V1.shape != K1.shape:
+        raise ValueError("shape mismatch between fresh rows and cache")
+    if not (k1.dtype == v1.dtype == K1.dtype == V1.dtype):
+        raise TypeError("k1, v1, K1, V1 must share a dtype")
+    if cand_pos.dtype != torch.int64 or not cand_pos.is_cuda or cand_pos.numel() != n or not cand_pos.is_contiguous():
+        raise ValueError("cand_pos must be a contiguous int64 CUDA tensor of length n")
+    dev = k1.device
+    if norms_out is None:
+        norms_out = torch.empty(2, H, n, dtype=torch.float32, device=dev)
+    elif norms_out.shape != (2, H, n) or norms_out.dtype != torch.float32 or not norms_out.is_contiguous():
+        raise ValueError("norms_out must be a contiguous fp32 [2, H, n] tensor")
+    if ws is None:
+        ws = workspace(dev, stream)
+    if n == 0:
+        return norms_out
+    with torch.cuda.device(dev):
+        rc = C.lib().tread_deviation_head_norms(
+            k1.data_ptr(), v1.data_ptr(), f_st, f_sh, K1.data_ptr(), V1.data_ptr(), c_st, c_sh, K1.shape[1],
+            cand_pos.data_ptr(), n, H, D, C.dtype_code(k1.dtype), norms_out.data_ptr(), ws.data_ptr(),
+            _stream_arg(stream, dev))
+    C.check(rc, "tread_deviation_head_norms")
+    return norms_out
+
+
+def select_head_norms(norms, cand_pos, budget, dev_out=None, sel_idx=None, sel_pos=None, ws=None, stream=None):
+    """Deviation and top-`budget` selection from every head's norms, fp32 [2, H, n] in global head
+    order (an all-gather of `deviation_head_norms` over the KV-head ranks). Same results as
+    `deviation_topk` on a single GPU holding all heads."""
+    C.require_cuda(norms, "norms")
+    if norms.dim() != 3 or norms.shape[0] != 2 or norms.dtype != torch.float32 or not norms.is_contiguous():
+        raise ValueError("norms must be a contiguous fp32 [2, H, n] tensor")
+    _, H, n = norms.shape
+    if cand_pos.dtype != torch.int64 or not cand_pos.is_cuda or cand_pos.numel() != n or not cand_pos.is_contiguous():
+        raise ValueError("cand_pos must be a contiguous int64 CUDA tensor of length n")
+    budget = int(budget)
+    if not 0 <= budget <= n:
+        raise ValueError(f"budget {budget} outside [0, {n}]")
+    dev = norms.device
+    if dev_out is None:
+        dev_out = torch.empty(n, dtype=torch.float32, device=dev)
+    if sel_idx is None:
+        sel_idx = torch.empty(budget, dtype=torch.int64, device=dev)
+    if sel_pos is None:
+        sel_pos = torch.empty(budget, dtype=torch.int64, device=dev)
+    if ws is None:
+        ws = workspace(dev, stream)
+    if n == 0:
+        return dev_out, sel_idx, sel_pos
+    with torch.cuda.device(dev):
+        rc = C.lib().tread_select_head_norms(
+            norms.data_ptr(), n, H, budget, cand_pos.data_ptr(), dev_out.data_ptr(),
+            sel_idx.data_ptr() if budget else None, sel_pos.data_ptr() if budget else None, ws.data_ptr(),
+            _stream_arg(stream, dev))
+    C.check(rc, "tread_select_head_norms")
+    return dev_out, sel_idx, sel_pos
+
+
 # ---- recompute rows: RoPE + K/V splice, attention -------------------------------------------
 
 def _layer_cache(K, name):

@@ -24,6 +24,7 @@ class Qwen2Rows:
     def __init__(self, model):
         cfg = model.config
         self.model = model
+        self.config = cfg
         self.L = cfg.num_hidden_layers
         self.hidden = cfg.hidden_size
         self.Hq = cfg.num_attention_heads
@@ -40,6 +41,7 @@ class Qwen2Rows:
             raise NotImplementedError(f"rope_type {rot.rope_type} is not supported")
         self.embed = model.model.embed_tokens.weight
         self.norm_w = model.model.norm.weight
+        self.norm_eps = model.model.norm.variance_epsilon
         self.lm_head = model.lm_head.weight
         self.layers = []
         with torch.no_grad():
@@ -105,8 +107,13 @@ class Qwen2Rows:
 
     def logits(self, h_last):
         """Final RMSNorm + lm_head of the given rows (HF Qwen2Model.norm, Qwen2ForCausalLM.lm_head)."""
-        x = self.rmsnorm(h_last, self.norm_w, self.model.model.norm.variance_epsilon)
+        x = self.rmsnorm(h_last, self.norm_w, self.norm_eps)
         return x @ self.lm_head.t()
+
+    def deviation_select(self, k1, v1, K1, V1, cand_pos, budget):
+        """Layer-1 deviation of the candidates and the top-`budget` selection (dev, sel_idx, S);
+        the KV-head tensor-parallel rows override this with the split selector."""
+        return kernels.deviation_topk(k1, v1, K1, V1, cand_pos, budget)
 
     def new_cache(self, T):
         """Zeroed per-request KV cache [L, 1, Hkv, T, D] for K and for V."""
