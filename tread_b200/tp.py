@@ -115,7 +115,11 @@ class TPQwen2Rows(Qwen2Rows):
     collectives. Build with `from_model` (slices an HF model's weights) or `random` (seeded
     random-init weights of a config, generated layer by layer on the device)."""
 
-    def __init__(self, cfg, layers, embed, norm_w, norm_eps, lm_head, group=None, dtype=None, device=None):
+    def __init__(self, cfg, layers, embed, norm_w, norm_eps, lm_head, group=None, dtype=None, device=None,
+                 rotary=None):
+        """rotary: the model's rotary-embedding module (its inv_freq buffer as the model holds it:
+        a model cast to bf16 carries bf16-rounded frequencies, and its own RoPE uses those);
+        default: a fresh fp32 one from `cfg`, as a model loaded in its dtype has."""
         from transformers.models.qwen2.modeling_qwen2 import Qwen2RotaryEmbedding
 
         self.model = None
@@ -134,7 +138,7 @@ class TPQwen2Rows(Qwen2Rows):
         self.eps = cfg.rms_norm_eps
         self.dtype = dtype or embed.dtype
         self.device = device or embed.device
-        rot = Qwen2RotaryEmbedding(config=cfg)
+        rot = rotary if rotary is not None else Qwen2RotaryEmbedding(config=cfg)
         if getattr(rot, "rope_type", "default") not in ("default", "linear", "llama3"):
             raise NotImplementedError(f"rope_type {rot.rope_type} is not supported")
         self.inv_freq = rot.inv_freq.float().cpu().tolist()
@@ -149,7 +153,7 @@ class TPQwen2Rows(Qwen2Rows):
         with torch.no_grad():
             return cls(model.config, (_hf_layer(layer) for layer in model.model.layers),
                        model.model.embed_tokens.weight, model.model.norm.weight, model.model.norm.variance_epsilon,
-                       model.lm_head.weight, group, model.dtype, model.device)
+                       model.lm_head.weight, group, model.dtype, model.device, model.model.rotary_emb)
 
     @classmethod
     def random(cls, cfg, group=None, seed=0, dtype=torch.bfloat16, device="cuda"):
