@@ -18,6 +18,9 @@ tread/blend.py:22-39). Algorithmic bytes per step = read K+V + write K+V = 939.5
 Multi-GPU: every rank assembles its own requests from its own pool (weak scaling, no
 collective on the data path).
 
+Serving leg (`serving_dp`): BASELINE configs[4], N replicas of the 7B model with doc blocks
+sharded by content hash (tread_b200.dp), requests/s of the whole job and TTFT percentiles.
+
 TTFT legs (objects on the same line): `ttft` (1 GPU) is the configs[2] 7B request through the
 single-GPU engine, graphed and eager, at ratios 0 / 0.2 / 0.5 / 1.0. `ttft_tp` is the model split
 over the N GPUs by KV head (tread_b200.tp, NCCL all-reduce after o_proj and down_proj): the
@@ -62,6 +65,8 @@ def parse():
     ap.add_argument("--only", choices=["attention", "selector"], default=None,
                     help="run one kernel microbench alone (for profiler captures) and print its timing")
     ap.add_argument("--ttft-reps", type=int, default=5, help="timed warm requests per recompute ratio")
+    ap.add_argument("--no-dp", action="store_true", help="skip the configs[4] hash-sharded replica serving leg")
+    ap.add_argument("--dp-rounds", type=int, default=12, help="timed serving rounds (one request per replica each)")
     ap.add_argument("--no-tp", action="store_true",
                     help="skip the KV-head tensor-parallel TTFT legs (configs[2] 7B, configs[3] 32B)")
     return ap.parse_args()
@@ -316,6 +321,7 @@ def run_gpu(args):
         if world > 1 and not args.no_ttft:
             ttft_tp["qwen2.5-7b"] = run_ttft_tp(args, dev, world, rank, "qwen2.5-7b", 256, 16, 496, 64)
         ttft_tp["qwen2.5-32b"] = run_ttft_tp(args, dev, world, rank, "qwen2.5-32b", 512, 32, 500, 128)
+    serving = None if args.no_dp else run_serving_dp(args, dev, world, rank)
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
@@ -341,6 +347,7 @@ def run_gpu(args):
             "selector": selector,
             "ttft": ttft,
             "ttft_tp": ttft_tp,
+            "serving_dp": serving,
             "gpu_launches": args.steps,
             "clocks": clk,
         }
@@ -510,6 +517,99 @@ def run_ttft_tp(args, dev, world, rank, arch, prefix_len, ndocs, doc_len, q_len)
                                             if torch.is_tensor(t)) / 1e9, 2),
            "ratios": res, "p50_ms_20pct": res["0.2"]["p50_ms"]}
     del eng, net
+    torch.cuda.empty_cache()
+    barrier(world)
+    return out
+
+
+def run_serving_dp(args, dev, world, rank):
+    """N data-parallel replicas of a random-init Qwen2.5-7B architecture
+    (bf16), doc blocks sharded by content hash (tread_b200.dp.ShardedEngine). Pool of 512 docs,
+    lengths uniform in [256, 2048], Zipf(s = 1.1) popularity (seeded, the same on every rank); each
+    request picks 8-24 docs by popularity in random order behind a shared 256-token system prompt,
+    plus a 64-token query; 20% recompute. Each replica's GPU block budget is 25% of its shard of
+    the pool's bytes, so the LRU spills to the pinned-host tier and fetches back.
+
+    The offered load is a closed loop: every replica serves one request per round (the rounds are
+    the exchange steps), so N requests are in flight. Untimed warm-up rounds fill the stores, then
+    --dp-rounds rounds are timed: TTFT per request by wall clock (host ids in, first token out),
+    requests/s = N x rounds / the max over ranks of the timed region's length."""
+    import torch.distributed as dist
+
+    from tread_b200 import BlockStore
+    from tread_b200.configs import random_model, random_tokens
+    from tread_b200.dp import ShardedEngine
+
+    model = random_model("qwen2.5-7b", dtype=torch.bfloat16, device=dev, seed=args.seed, init_on_device=True)
+    cfg = model.config
+    V = cfg.vocab_size
+    g = torch.Generator().manual_seed(args.seed + 21)
+    lens = torch.randint(256, 2049, (512,), generator=g)
+    pool = [random_tokens(int(n), V, g) for n in lens]
+    prefix = random_tokens(256, V, g)
+    popularity = torch.randperm(512, generator=g)  # doc popularity[i] has Zipf rank i
+    w = torch.empty(512)
+    w[popularity] = 1.0 / torch.arange(1, 513, dtype=torch.float64).pow(1.1).float()
+    per_tok = cfg.num_hidden_layers * cfg.num_key_value_heads * (cfg.hidden_size // cfg.num_attention_heads) * 2 * 2
+    pool_bytes = int(lens.sum()) * per_tok
+    gpu_budget = int(0.25 * pool_bytes / world)
+    eng = ShardedEngine(model, BlockStore(gpu_budget, pool_bytes))
+    rg = torch.Generator().manual_seed(args.seed + 1000 + rank)  # this replica's client stream
+
+    def request():
+        k = int(torch.randint(8, 25, (1,), generator=rg))
+        idx = torch.multinomial(w, k, replacement=False, generator=rg)
+        return [pool[i] for i in idx.tolist()], random_tokens(64, V, rg)
+
+    warm = 6
+    ttft, st_all = [], []
+    s0 = None
+    for rnd in range(warm + args.dp_rounds):
+        if rnd == warm:
+            barrier(world)
+            torch.cuda.synchronize(dev)
+            t_start = time.perf_counter()
+            s0 = dict(vars(eng.store.stats))
+            b0 = (eng.shards.sent_bytes, eng.shards.recv_bytes)
+        docs, query = request()
+        t0 = time.perf_counter()
+        logits, cache, st = eng.serve(prefix, docs, query, ratio=0.2)
+        int(logits.argmax().item())
+        t1 = time.perf_counter()
+        del cache
+        if rnd >= warm:
+            ttft.append(t1 - t0)
+            st_all.append(st)
+    torch.cuda.synchronize(dev)
+    elapsed = max_over_ranks(time.perf_counter() - t_start, world, dev)
+    s1 = vars(eng.store.stats)
+    d = {k: s1[k] - s0[k] for k in ("hits", "misses", "evictions", "cpu_hits", "offloads")}
+    t = torch.tensor(ttft, dtype=torch.float64, device=dev)
+    req_hits = sum(s_.hits for s_ in st_all)
+    req_blocks = sum(s_.hits + s_.misses for s_ in st_all)
+    peer = float(eng.shards.sent_bytes - b0[0])
+    if world > 1:
+        parts = [torch.empty_like(t) for _ in range(world)]
+        dist.all_gather(parts, t)
+        t = torch.cat(parts)
+        tot = torch.tensor([d["hits"], d["misses"], d["cpu_hits"], d["offloads"], peer, req_hits, req_blocks],
+                           dtype=torch.float64, device=dev)
+        dist.all_reduce(tot)
+        d["hits"], d["misses"], d["cpu_hits"], d["offloads"], peer, req_hits, req_blocks = tot.tolist()
+    t = t.cpu().sort().values
+    n_req = world * args.dp_rounds
+    out = {"workload": "configs[4] 7B replicas, 512-doc pool (256-2048 tokens, Zipf 1.1), 8-24 docs + 256 prefix "
+                       "+ 64 query, 20% recompute, GPU budget 25% of each hash shard",
+           "replicas": world, "rounds": args.dp_rounds, "warmup_rounds": warm,
+           "requests_per_s": round(n_req / elapsed, 2),
+           "ttft_p50_ms": round(float(t[len(t) // 2]) * 1e3, 2),
+           "ttft_p99_ms": round(float(t[min(len(t) - 1, int(0.99 * len(t)))]) * 1e3, 2),
+           "store_lookups": {"hits": int(d["hits"]), "misses": int(d["misses"]), "cpu_tier_hits": int(d["cpu_hits"]),
+                             "offloads": int(d["offloads"])},
+           "request_block_hit_rate": round(req_hits / max(1, req_blocks), 4),
+           "peer_copy_mb_per_request": round(peer / n_req / 1e6, 1),
+           "pool_gb": round(pool_bytes / 1e9, 1), "gpu_budget_gb_per_replica": round(gpu_budget / 1e9, 2)}
+    del eng, model
     torch.cuda.empty_cache()
     barrier(world)
     return out

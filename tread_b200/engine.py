@@ -151,6 +151,13 @@ class Engine:
         prefix_ids, docs, query_ids = devs[0], devs[1:-1], devs[-1]
         pkey, pb = self.prefix_block(prefix_ids, st, namespace, host_ids=host[0])
         blocks = self.doc_blocks(pkey, pb, docs, st, host_docs=host[1:-1])
+        return self._run_request(st, t0, prefix_ids, docs, query_ids, pb, blocks, ratio, policy)
+
+    def _run_request(self, st, t0, prefix_ids, docs, query_ids, pb, blocks, ratio, policy):
+        """Assembly of the prefix block `pb` and the doc `blocks` (device ids), then selection,
+        the recompute + query rows and the first-token logits; fills the stage timers of `st`
+        (t0: the request's start) and returns (logits, DynamicCache, st)."""
+        net = self.net
         P = pb.n_tokens
         nq = len(query_ids)
         T = P + sum(len(d) for d in docs)
