@@ -49,7 +49,7 @@ def _worker(rank, port, q):
                 rnd.append(([pool[i] for i in idx], torch.randint(0, 4096, (8,), generator=g)))
             rounds.append(rnd)
         # small GPU shard budget so blocks spill to the pinned tier and come back
-        eng = ShardedEngine(model, BlockStore(6 << 20, 1 << 30))
+        eng = ShardedEngine(model, BlockStore(1 << 20, 1 << 30))
         ref = Engine(model, BlockStore(1 << 34))
         kls, hits = [], 0
         for i, rnd in enumerate(rounds):
