@@ -58,7 +58,7 @@ def _worker(rank, world, port, budget, cpu_budget, q):
         os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
         dist.init_process_group("gloo", rank=rank, world_size=world)
         store = BlockStore(budget, cpu_budget)
-        sh = HashShardedBlocks(store, make_prefix, make_doc, empty_block)
+        sh = HashShardedBlocks(store, make_prefix, lambda ids, pb: [make_doc(x, pb) for x in ids], empty_block)
         seen = set()
         ok, why = True, ""
         for rnd in _requests(world, 10):

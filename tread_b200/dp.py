@@ -43,12 +43,13 @@ class HashShardedBlocks:
     """The per-round block exchange of hash-sharded replicas.
 
     store: this rank's BlockStore (its shard). make_prefix(ids) -> (K, V) computes a prefix block;
-    make_doc(ids, prefix_block) -> (K, V) computes a doc block behind its prefix; empty_block(n)
-    -> (K, V) allocates receive buffers for an n-token block. ids are int64 numpy arrays."""
+    make_docs([ids, ...], prefix_block) -> [(K, V), ...] computes doc blocks behind their prefix
+    (all of a round's missing docs under one prefix in one call); empty_block(n) -> (K, V)
+    allocates receive buffers for an n-token block. ids are int64 numpy arrays."""
 
-    def __init__(self, store, make_prefix, make_doc, empty_block, group=None):
+    def __init__(self, store, make_prefix, make_docs, empty_block, group=None):
         self.store = store
-        self.make_prefix, self.make_doc, self.empty_block = make_prefix, make_doc, empty_block
+        self.make_prefix, self.make_docs, self.empty_block = make_prefix, make_docs, empty_block
         self.group = group
         self.world = dist.get_world_size(group) if dist.is_initialized() else 1
         self.rank = dist.get_rank(group) if dist.is_initialized() else 0
@@ -133,12 +134,16 @@ class HashShardedBlocks:
         self._exchange(sorted((k, r) for k, rs in need.items() for r in rs if r != self._owner(k)), have,
                        {k: len(v) for k, v in prefix_ids.items()}, {k: 0 for k in prefix_ids})
 
-        # doc blocks: prefilled by their owners behind their prefix, then to their users
+        # doc blocks: prefilled by their owners behind their prefix (one batch per prefix), then
+        # to their users
+        todo = defaultdict(list)
         for dkey in sorted(doc_of):
             if self._owner(dkey) == self.rank and not hit[dkey]:
-                pkey, ids = doc_of[dkey]
-                pb = have[pkey]
-                K, V = self.make_doc(ids, pb)
+                todo[doc_of[dkey][0]].append(dkey)
+        for pkey in sorted(todo):
+            pb = have[pkey]
+            made = self.make_docs([doc_of[k][1] for k in todo[pkey]], pb)
+            for dkey, (K, V) in zip(todo[pkey], made):
                 have[dkey] = self._put(dkey, K, V, pb.n_tokens)
         self._exchange(sorted((k, r) for k in doc_of for r in users[k] if r != self._owner(k)), have,
                        {k: len(v[1]) for k, v in doc_of.items()},
@@ -158,7 +163,7 @@ class ShardedEngine(Engine):
 
     def __init__(self, model, store, group=None):
         super().__init__(model, store, graphs=False)
-        self.shards = HashShardedBlocks(store, self._make_prefix, self._make_doc, self._empty_block, group)
+        self.shards = HashShardedBlocks(store, self._make_prefix, self._make_docs, self._empty_block, group)
 
     def _ids(self, ids):
         return torch.from_numpy(np.ascontiguousarray(ids, dtype=np.int64)).to(self.net.device)
@@ -166,11 +171,8 @@ class ShardedEngine(Engine):
     def _make_prefix(self, ids):
         return self._prefill_rows(self._ids(ids))
 
-    def _make_doc(self, ids, pb):
-        P = pb.n_tokens
-        pb.wait()
-        Kf, Vf = self._prefill_rows(self._ids(ids), (pb.K, pb.V), P)
-        return Kf[..., P:, :].contiguous(), Vf[..., P:, :].contiguous()
+    def _make_docs(self, ids_list, pb):
+        return self._prefill_docs([self._ids(ids) for ids in ids_list], pb)
 
     def _empty_block(self, n):
         shape = (self.net.L, 1, self.net.Hkv, n, self.net.D)

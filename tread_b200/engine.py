@@ -96,6 +96,37 @@ class Engine:
         net.run(net.embed_ids(ids), pos, list(K.unbind(0)), list(V.unbind(0)))
         return K, V
 
+    def _prefill_docs(self, docs, pb, max_rows=16384):
+        """K/V blocks [L, 1, Hkv, n_i, D] of several docs, each computed at positions P.. behind
+        the prefix block `pb`, seeing the prefix and itself only: the block-diagonal packed
+        prefill of tread/engine.py:59-96. Docs go through the layers together, up to `max_rows`
+        rows per pass: the projections and the MLP run once over all their rows, and RoPE + splice
+        and attention run per doc against its own [prefix | doc] cache."""
+        net = self.net
+        P = pb.n_tokens
+        pb.wait()
+        out, i = [], 0
+        while i < len(docs):
+            group = [docs[i]]
+            rows = len(docs[i])
+            i += 1
+            while i < len(docs) and rows + len(docs[i]) <= max_rows:
+                group.append(docs[i])
+                rows += len(docs[i])
+                i += 1
+            segs, r0 = [], 0
+            for d in group:
+                K, V = net.new_cache(P + len(d))
+                if P:
+                    kernels.rope_gather_append([(pb.K, pb.V, 0, 0)], K, V, net.inv_freq, net.attn_scaling)
+                segs.append((r0, r0 + len(d), torch.arange(P, P + len(d), device=d.device), K, V))
+                r0 += len(d)
+            h = net.embed_ids(torch.cat(group))
+            for l in range(net.L):
+                h = net.layer_segments(l, h, [(a, b, pos, K[l], V[l]) for a, b, pos, K, V in segs])
+            out.extend((K[..., P:, :].contiguous(), V[..., P:, :].contiguous()) for _, _, _, K, V in segs)
+        return out
+
     @torch.inference_mode()
     def prefix_block(self, prefix_ids, st, namespace="", host_ids=None):
         # Doc keys derive from this key, so a namespace isolates a tenant's whole block tree.
@@ -116,7 +147,8 @@ class Engine:
         """Look up every doc's block; prefill the misses after the cached prefix (tread/engine.py:59-96).
 
         Each missed doc runs at positions P.. over [prefix KV | its own KV], so it sees the prefix
-        and itself, never another doc: the reference's block-diagonal packed prefill, per doc.
+        and itself, never another doc: the reference's block-diagonal packed prefill, with all
+        missed docs in one pass (`_prefill_docs`).
         """
         keys = [block_key(*self.sig, prefix_key, d) for d in (docs if host_docs is None else host_docs)]
         blocks = [self.store.get(k, wait=False) for k in keys]
@@ -127,11 +159,9 @@ class Engine:
             return blocks
         st.misses += len(miss)
         P = pb.n_tokens
-        pb.wait()
-        for i in miss:
+        made = self._prefill_docs([docs[i].to(self.net.device) for i in miss], pb)
+        for i, (K, V) in zip(miss, made):
             st.tokens_prefilled += len(docs[i])
-            Kf, Vf = self._prefill_rows(docs[i].to(self.net.device), (pb.K, pb.V), P)
-            K, V = Kf[..., P:, :].contiguous(), Vf[..., P:, :].contiguous()
             blocks[i] = self.store.put(keys[i], K, V, P) or _Tmp(K, V, P)
         return blocks
 

@@ -84,16 +84,29 @@ class Qwen2Rows:
 
     def layer(self, l, h, pos, K, V, qkv=None):
         """h: [R, hidden] rows at positions pos (int64 [R]); K, V: layer-l caches [1, Hkv, T, D]
-        (or [Hkv, T, D]); the rows' k/v are written into them. The residual stream is updated in
-        place (h is returned)."""
-        p = self.layers[l]
+        (or [Hkv, T, D]); the rows' k/v are written into them. Returns the new residual rows
+        (for this class: h itself, updated in place)."""
+        return self.layer_segments(l, h, [(0, h.shape[0], pos, K, V)], qkv)
+
+    def layer_segments(self, l, h, segs, qkv=None):
+        """One layer over rows that belong to independent caches: segs = [(r0, r1, pos, K, V)],
+        rows r0..r1-1 of h sit at positions pos and read/write cache K, V. The projections and the
+        MLP run once over all rows; RoPE + splice and attention run per segment."""
         R = h.shape[0]
         if qkv is None:
             qkv = self.qkv(l, h)
         q = torch.empty(R, self.Hq, self.D, dtype=h.dtype, device=h.device)
-        kernels.rope_rows(qkv, pos, self.Hq, self.Hkv, self.D, q, K, V, self.inv_freq, self.attn_scaling, self.err)
-        o = kernels.attn_rows(q, K, V, pos, err=self.err)
-        h.addmm_(o.view(R, -1), p["wo"].t())
+        o = torch.empty_like(q)
+        for r0, r1, pos, K, V in segs:
+            kernels.rope_rows(qkv[r0:r1], pos, self.Hq, self.Hkv, self.D, q[r0:r1], K, V, self.inv_freq,
+                              self.attn_scaling, self.err)
+            kernels.attn_rows(q[r0:r1], K, V, pos, out=o[r0:r1], err=self.err)
+        return self.layer_tail(l, h, o.view(R, -1))
+
+    def layer_tail(self, l, h, o):
+        """h + o_proj(o), then h + down(silu(gate) * up) of its RMSNorm (residuals in place)."""
+        p = self.layers[l]
+        h.addmm_(o, p["wo"].t())
         x = self.rmsnorm(h, p["ln2"], p["ln2_eps"])
         a = kernels.silu_mul(x @ p["wgu"].t())
         return h.addmm_(a, p["wd"].t())

@@ -175,17 +175,11 @@ class TPQwen2Rows(Qwen2Rows):
             dist.all_reduce(out, group=self.group)
         return out
 
-    def layer(self, l, h, pos, K, V, qkv=None):
-        """As Qwen2Rows.layer over this rank's heads; returns the new residual rows (a new tensor,
-        identical on every rank)."""
+    def layer_tail(self, l, h, o):
+        """Row-parallel o_proj and down_proj with their all-reduces; returns the new residual rows
+        (a new tensor, identical on every rank)."""
         p = self.layers[l]
-        R = h.shape[0]
-        if qkv is None:
-            qkv = self.qkv(l, h)
-        q = torch.empty(R, self.Hq, self.D, dtype=h.dtype, device=h.device)
-        kernels.rope_rows(qkv, pos, self.Hq, self.Hkv, self.D, q, K, V, self.inv_freq, self.attn_scaling, self.err)
-        o = kernels.attn_rows(q, K, V, pos, err=self.err)
-        h = self._row_parallel(o.view(R, -1), p["wo"], h)
+        h = self._row_parallel(o, p["wo"], h)
         x = self.rmsnorm(h, p["ln2"], p["ln2_eps"])
         a = kernels.silu_mul(x @ p["wgu"].t())
         return self._row_parallel(a, p["wd"], h)
