@@ -97,26 +97,63 @@ __device__ __forceinline__ unsigned block_exclusive_sum(unsigned v, unsigned* s_
   return r;
 }
 
+// Adds 1 to hist[bin] for every lane with `act`; lanes that share a bin add once, together
+// (the top digits of nearby fp32 values coincide, so per-lane atomics would serialise on one
+// bin). All 32 lanes of the warp must call it.
+__device__ __forceinline__ void hist_add(unsigned* hist, bool act, unsigned bin) {
+  const unsigned b = act ? bin : 0x100u;
+  const unsigned peers = __match_any_sync(0xffffffffu, b);
+  if (act && (threadIdx.x & 31) == (unsigned)(__ffs(peers) - 1)) atomicAdd(&hist[bin], (unsigned)__popc(peers));
+}
+
+constexpr int kKeyCache = 16;  // keys per thread kept in registers when n <= kThreads * kKeyCache
+
 // Top-`budget` of dev[0..n) (largest first, lower index wins ties), written ascending by index.
 // Thread t owns the contiguous index chunk [t*C, (t+1)*C): MSB-first radix select over 8-bit
-// digits (histogram, then a suffix scan over the 256 bins by threads 0..255), then one pass of
-// per-chunk counts and two block scans place every selected index.
-__device__ void select_topk(const float* dev, int n, int budget, const int64_t* cand_pos, int64_t* sel_idx,
-                            int64_t* sel_pos) {
+// digits (warp-aggregated histogram, then a suffix scan over the 256 bins by threads 0..255),
+// then one pass of per-chunk counts and two block scans place every selected index. With
+// C <= kKeyCache the thread's keys stay in registers for all passes; otherwise every pass
+// re-reads them from L2.
+template <bool CACHED>
+__device__ void select_topk_impl(const float* dev, int n, int budget, const int64_t* cand_pos, int64_t* sel_idx,
+                                 int64_t* sel_pos) {
   __shared__ unsigned hist[256];
   __shared__ unsigned s_scan[kWarps + 1];
   __shared__ unsigned s_digit, s_rem;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int C = (n + kThreads - 1) / kThreads;
   const int lo = min(n, tid * C), hi = min(n, lo + C);
+  constexpr int KC = CACHED ? kKeyCache : 1;
+  unsigned kc[KC];
+  if constexpr (CACHED) {
+#pragma unroll
+    for (int k = 0; k < KC; ++k) kc[k] = (k < C && lo + k < hi) ? order_key(__ldcg(dev + lo + k)) : 0u;
+  }
+  auto key_at = [&](int k) -> unsigned {
+    if constexpr (CACHED) {
+      return kc[k];
+    } else {
+      return order_key(__ldcg(dev + lo + k));
+    }
+  };
   unsigned prefix = 0u, mask = 0u, remaining = (unsigned)budget;
 #pragma unroll 1
   for (int shift = 24; shift >= 0; shift -= 8) {
     if (tid < 256) hist[tid] = 0u;
     __syncthreads();
-    for (int i = lo; i < hi; ++i) {
-      const unsigned key = order_key(__ldcg(dev + i));
-      if ((key & mask) == prefix) atomicAdd(&hist[(key >> shift) & 255u], 1u);
+    if constexpr (CACHED) {
+#pragma unroll
+      for (int k = 0; k < KC; ++k) {
+        if (k >= C) break;  // C is the same for every thread: the warp stays converged
+        const unsigned key = kc[k];
+        hist_add(hist, lo + k < hi && (key & mask) == prefix, (key >> shift) & 255u);
+      }
+    } else {
+      for (int k = 0; k < C; ++k) {
+        const bool valid = lo + k < hi;
+        const unsigned key = valid ? key_at(k) : 0u;
+        hist_add(hist, valid && (key & mask) == prefix, (key >> shift) & 255u);
+      }
     }
     __syncthreads();
     // thread j < 256 handles bin 255 - j: its inclusive prefix over j is the count of keys whose
@@ -150,29 +187,52 @@ __device__ void select_topk(const float* dev, int n, int budget, const int64_t* 
   // prefix is the key of the budget-th largest value; `remaining` of its ties are taken, lowest
   // indices first.
   unsigned gt = 0u, eq = 0u;
-  for (int i = lo; i < hi; ++i) {
-    const unsigned key = order_key(__ldcg(dev + i));
+  auto count = [&](int k) {
+    const unsigned key = key_at(k);
     gt += key > prefix;
     eq += key == prefix;
+  };
+  if constexpr (CACHED) {
+#pragma unroll
+    for (int k = 0; k < KC; ++k)
+      if (lo + k < hi) count(k);
+  } else {
+    for (int k = 0; lo + k < hi; ++k) count(k);
   }
   unsigned tot;
   const unsigned eq_before = block_exclusive_sum(eq, s_scan, tot);
   const unsigned take_eq = eq_before >= remaining ? 0u : min(eq, remaining - eq_before);
   unsigned r = block_exclusive_sum(gt + take_eq, s_scan, tot);
   unsigned taken = 0u;
-  for (int i = lo; i < hi; ++i) {
-    const unsigned key = order_key(__ldcg(dev + i));
+  auto place = [&](int k) {
+    const unsigned key = key_at(k);
     bool sel = key > prefix;
     if (key == prefix && taken < take_eq) {
       sel = true;
       ++taken;
     }
     if (sel) {
+      const int i = lo + k;
       sel_idx[r] = i;
       if (sel_pos) sel_pos[r] = cand_pos[i];
       ++r;
     }
+  };
+  if constexpr (CACHED) {
+#pragma unroll
+    for (int k = 0; k < KC; ++k)
+      if (lo + k < hi) place(k);
+  } else {
+    for (int k = 0; lo + k < hi; ++k) place(k);
   }
+}
+
+__device__ void select_topk(const float* dev, int n, int budget, const int64_t* cand_pos, int64_t* sel_idx,
+                            int64_t* sel_pos) {
+  if (n <= kThreads * kKeyCache)
+    select_topk_impl<true>(dev, n, budget, cand_pos, sel_idx, sel_pos);
+  else
+    select_topk_impl<false>(dev, n, budget, cand_pos, sel_idx, sel_pos);
 }
 
 template <typename T, int E>
