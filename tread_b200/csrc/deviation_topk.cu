@@ -109,14 +109,16 @@ __device__ __forceinline__ void hist_add(unsigned* hist, bool act, unsigned bin)
 constexpr int kKeyCache = 16;  // keys per thread kept in registers when n <= kThreads * kKeyCache
 
 // Top-`budget` of dev[0..n) (largest first, lower index wins ties), written ascending by index.
-// Thread t owns the contiguous index chunk [t*C, (t+1)*C): MSB-first radix select over 8-bit
-// digits (warp-aggregated histogram, then a suffix scan over the 256 bins by threads 0..255),
-// then one pass of per-chunk counts and two block scans place every selected index. With
-// C <= kKeyCache the thread's keys stay in registers for all passes; otherwise every pass
-// re-reads them from L2.
+// Thread t owns the contiguous index chunk [t*C, (t+1)*C). With C <= kKeyCache the thread's keys
+// stay in registers and the threshold key is found by narrowing a value interval (below); larger
+// inputs re-read their keys from L2 each pass and run an MSB-first radix select over 8-bit digits
+// (warp-aggregated histogram). Either way a suffix scan over 256 bins by threads 0..255 picks the
+// bucket each pass, then one pass of per-chunk counts and two block scans place every selected
+// index.
 template <bool CACHED>
-__device__ void select_topk_impl(const float* dev, int n, int budget, const int64_t* cand_pos, int64_t* sel_idx,
-                                 int64_t* sel_pos) {
+__device__ void select_topk_impl(const float* __restrict__ dev, int n, int budget,
+                                 const int64_t* __restrict__ cand_pos, int64_t* __restrict__ sel_idx,
+                                 int64_t* __restrict__ sel_pos) {
   __shared__ unsigned hist[256];
   __shared__ unsigned s_scan[kWarps + 1];
   __shared__ unsigned s_digit, s_rem;
@@ -136,53 +138,113 @@ __device__ void select_topk_impl(const float* dev, int n, int budget, const int6
       return order_key(__ldcg(dev + lo + k));
     }
   };
-  unsigned prefix = 0u, mask = 0u, remaining = (unsigned)budget;
-#pragma unroll 1
-  for (int shift = 24; shift >= 0; shift -= 8) {
-    if (tid < 256) hist[tid] = 0u;
-    __syncthreads();
-    if constexpr (CACHED) {
+  unsigned prefix = 0u, remaining = (unsigned)budget;
+  if constexpr (CACHED) {
+    // Narrow a key interval [L, U] that holds the budget-th largest key: bucket the keys inside it
+    // into 256 equal-width buckets, keep the bucket that holds it, until L == U. Buckets of the
+    // values' own range spread even nearly equal floats (fixed 8-bit digits would put them all in
+    // one bin), so per-lane shared atomics rarely collide; at most 4 passes.
+    __shared__ unsigned s_min[kWarps], s_max[kWarps];
+    unsigned kmin = 0xffffffffu, kmax = 0u;
 #pragma unroll
-      for (int k = 0; k < KC; ++k) {
-        if (k >= C) break;  // C is the same for every thread: the warp stays converged
-        const unsigned key = kc[k];
-        hist_add(hist, lo + k < hi && (key & mask) == prefix, (key >> shift) & 255u);
+    for (int k = 0; k < KC; ++k)
+      if (lo + k < hi) {
+        kmin = min(kmin, kc[k]);
+        kmax = max(kmax, kc[k]);
       }
-    } else {
+    kmin = __reduce_min_sync(0xffffffffu, kmin);
+    kmax = __reduce_max_sync(0xffffffffu, kmax);
+    if (lane == 0) {
+      s_min[warp] = kmin;
+      s_max[warp] = kmax;
+    }
+    __syncthreads();
+    unsigned L = 0xffffffffu, U = 0u;
+#pragma unroll 1
+    for (int w = 0; w < kWarps; ++w) {
+      L = min(L, s_min[w]);
+      U = max(U, s_max[w]);
+    }
+    while (L < U) {
+      const unsigned span = U - L;
+      const int bits = 32 - __clz(span);
+      const int shift = bits > 8 ? bits - 8 : 0;  // (U - L) >> shift < 256
+      if (tid < 256) hist[tid] = 0u;
+      __syncthreads();
+#pragma unroll
+      for (int k = 0; k < KC; ++k)
+        if (lo + k < hi && kc[k] >= L && kc[k] <= U) atomicAdd(&hist[(kc[k] - L) >> shift], 1u);
+      __syncthreads();
+      unsigned c = 0u, incl = 0u;
+      if (tid < 256) {  // thread j takes bucket 255 - j: its inclusive prefix counts keys in buckets >= it
+        c = hist[255 - tid];
+        incl = c;
+#pragma unroll
+        for (int off = 1; off < 32; off <<= 1) {
+          const unsigned o = __shfl_up_sync(0xffffffffu, incl, off);
+          if (lane >= off) incl += o;
+        }
+        if (lane == 31) s_scan[warp] = incl;
+      }
+      __syncthreads();
+      if (tid < 256) {
+        for (int w = 0; w < warp; ++w) incl += s_scan[w];
+        const unsigned above = incl - c;
+        if (above < remaining && incl >= remaining) {
+          s_digit = 255u - (unsigned)tid;
+          s_rem = remaining - above;
+        }
+      }
+      __syncthreads();
+      const unsigned b = s_digit;
+      remaining = s_rem;
+      const unsigned nl = L + (b << shift);
+      const unsigned top = nl + ((1u << shift) - 1u);
+      U = top < nl ? U : min(U, top);  // (no wrap: nl + width - 1 stays below 2^32 within [L, U])
+      L = nl;
+      __syncthreads();
+    }
+    prefix = L;
+  } else {
+    unsigned mask = 0u;
+#pragma unroll 1
+    for (int shift = 24; shift >= 0; shift -= 8) {
+      if (tid < 256) hist[tid] = 0u;
+      __syncthreads();
       for (int k = 0; k < C; ++k) {
         const bool valid = lo + k < hi;
         const unsigned key = valid ? key_at(k) : 0u;
         hist_add(hist, valid && (key & mask) == prefix, (key >> shift) & 255u);
       }
-    }
-    __syncthreads();
-    // thread j < 256 handles bin 255 - j: its inclusive prefix over j is the count of keys whose
-    // digit is >= that bin
-    unsigned c = 0u, incl = 0u;
-    if (tid < 256) {
-      c = hist[255 - tid];
-      incl = c;
+      __syncthreads();
+      // thread j < 256 handles bin 255 - j: its inclusive prefix over j is the count of keys whose
+      // digit is >= that bin
+      unsigned c = 0u, incl = 0u;
+      if (tid < 256) {
+        c = hist[255 - tid];
+        incl = c;
 #pragma unroll
-      for (int off = 1; off < 32; off <<= 1) {
-        const unsigned o = __shfl_up_sync(0xffffffffu, incl, off);
-        if (lane >= off) incl += o;
+        for (int off = 1; off < 32; off <<= 1) {
+          const unsigned o = __shfl_up_sync(0xffffffffu, incl, off);
+          if (lane >= off) incl += o;
+        }
+        if (lane == 31) s_scan[warp] = incl;
       }
-      if (lane == 31) s_scan[warp] = incl;
-    }
-    __syncthreads();
-    if (tid < 256) {
-      for (int w = 0; w < warp; ++w) incl += s_scan[w];
-      const unsigned above = incl - c;
-      if (above < remaining && incl >= remaining) {
-        s_digit = 255u - (unsigned)tid;
-        s_rem = remaining - above;
+      __syncthreads();
+      if (tid < 256) {
+        for (int w = 0; w < warp; ++w) incl += s_scan[w];
+        const unsigned above = incl - c;
+        if (above < remaining && incl >= remaining) {
+          s_digit = 255u - (unsigned)tid;
+          s_rem = remaining - above;
+        }
       }
+      __syncthreads();
+      prefix |= s_digit << shift;
+      mask |= 255u << shift;
+      remaining = s_rem;
+      __syncthreads();
     }
-    __syncthreads();
-    prefix |= s_digit << shift;
-    mask |= 255u << shift;
-    remaining = s_rem;
-    __syncthreads();
   }
   // prefix is the key of the budget-th largest value; `remaining` of its ties are taken, lowest
   // indices first.
@@ -204,6 +266,34 @@ __device__ void select_topk_impl(const float* dev, int n, int budget, const int6
   const unsigned take_eq = eq_before >= remaining ? 0u : min(eq, remaining - eq_before);
   unsigned r = block_exclusive_sum(gt + take_eq, s_scan, tot);
   unsigned taken = 0u;
+  if constexpr (CACHED) {
+    // selection as a bit mask first, then the writes: every cand_pos load can be in flight at once
+    unsigned selm = 0u;
+#pragma unroll
+    for (int k = 0; k < KC; ++k) {
+      if (lo + k < hi) {
+        const unsigned key = kc[k];
+        bool sel = key > prefix;
+        if (key == prefix && taken < take_eq) {
+          sel = true;
+          ++taken;
+        }
+        selm |= (sel ? 1u : 0u) << k;
+      }
+    }
+#pragma unroll
+    for (int k = 0; k < KC; ++k)
+      if ((selm >> k) & 1u) sel_idx[r + __popc(selm & ((1u << k) - 1u))] = lo + k;
+    if (sel_pos) {
+      int64_t cp[KC];
+#pragma unroll
+      for (int k = 0; k < KC; ++k) cp[k] = ((selm >> k) & 1u) ? __ldg(cand_pos + lo + k) : 0;
+#pragma unroll
+      for (int k = 0; k < KC; ++k)
+        if ((selm >> k) & 1u) sel_pos[r + __popc(selm & ((1u << k) - 1u))] = cp[k];
+    }
+    return;
+  }
   auto place = [&](int k) {
     const unsigned key = key_at(k);
     bool sel = key > prefix;
@@ -218,13 +308,7 @@ __device__ void select_topk_impl(const float* dev, int n, int budget, const int6
       ++r;
     }
   };
-  if constexpr (CACHED) {
-#pragma unroll
-    for (int k = 0; k < KC; ++k)
-      if (lo + k < hi) place(k);
-  } else {
-    for (int k = 0; lo + k < hi; ++k) place(k);
-  }
+  for (int k = 0; lo + k < hi; ++k) place(k);
 }
 
 __device__ void select_topk(const float* dev, int n, int budget, const int64_t* cand_pos, int64_t* sel_idx,
@@ -243,8 +327,7 @@ __global__ void __launch_bounds__(kThreads, 2)
                           float* __restrict__ dev_out, int64_t* __restrict__ sel_idx, int64_t* __restrict__ sel_pos,
                           unsigned* __restrict__ workspace) {
   const int lane = threadIdx.x & 31;
-  const int t = blockIdx.x * kWarps + (threadIdx.x >> 5);
-  if (t < n) {
+  for (int t = blockIdx.x * kWarps + (threadIdx.x >> 5); t < n; t += gridDim.x * kWarps) {
     const long long pos = cand_pos[t];
     float dev;
     if (pos < 0 || pos >= T_cache) {
@@ -281,7 +364,7 @@ __global__ void __launch_bounds__(kThreads, 2)
   }
   if (budget <= 0) return;
   __shared__ bool s_last;
-  __threadfence();
+  if (lane == 0) __threadfence();  // this warp's dev writes, before the CTA's ticket
   __syncthreads();
   if (threadIdx.x == 0) s_last = atomicAdd(workspace, 1u) == gridDim.x - 1;
   __syncthreads();
@@ -291,11 +374,25 @@ __global__ void __launch_bounds__(kThreads, 2)
   if (threadIdx.x == 0) workspace[0] = 0u;  // ready for the next call
 }
 
+// Resident CTAs of the deviation kernel on the current device (2 per SM by its launch bounds).
+int resident_ctas() {
+  static int cache[128] = {0};
+  int d = 0;
+  if (cudaGetDevice(&d) != cudaSuccess || d < 0 || d >= 128) return 296;
+  if (!cache[d]) {
+    int sms = 0;
+    if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, d) != cudaSuccess || sms <= 0) sms = 148;
+    cache[d] = 2 * sms;
+  }
+  return cache[d];
+}
+
 template <typename T, int E>
 int launch_dev(const void* k1, const void* v1, long long f_st, long long f_sh, const void* K1, const void* V1,
                long long c_st, long long c_sh, long long T_cache, const int64_t* cand_pos, int n, int H, int budget,
                float* dev_out, int64_t* sel_idx, int64_t* sel_pos, unsigned* ws, cudaStream_t st) {
-  const int grid = (n + kWarps - 1) / kWarps;
+  // one wave: every warp loops over candidates, no partly filled second wave
+  const int grid = std::min((n + kWarps - 1) / kWarps, resident_ctas());
   deviation_topk_kernel<T, E><<<grid, kThreads, 0, st>>>(
       static_cast<const T*>(k1), static_cast<const T*>(v1), f_st, f_sh, static_cast<const T*>(K1),
       static_cast<const T*>(V1), c_st, c_sh, T_cache, cand_pos, n, H, budget, dev_out, sel_idx, sel_pos, ws);
