@@ -10,22 +10,24 @@
 //     tiles into separate 2-stage rings (two steps ahead of the MMAs that read them) straight
 //     from the [R, Hq, D] queries and the [Hkv, T, D] cache, refilling a stage when the MMA that
 //     read it commits to that stage's "free" barrier;
-//   - MMA issuer (lane 0 of warp 8): issues
-//     S_j = Q K_j^T (8 x tcgen05.mma kind::f16, M=N=K=128) into one of two TMEM S
-//     buffers, so the MMA of step j+1 runs while the rows are still in the softmax of step j,
-//     and O += P_j V_j into the TMEM accumulator once P_j is in shared memory;
-//   - softmax (warps 0-7; a row = a TMEM lane, its 128 columns split over two warps that swap
-//     partial maxima in shared memory): reads S once with tcgen05.ld into registers, masks keys
-//     past the row's position (only on tiles that reach it), keeps the running max and sum in
-//     the exp2 domain (ex2.approx, scale folded into one FMA), rescales O
-//     in TMEM only when the max grows by more than 8 (a stale max is exact since 1/l uses the
+//   - MMA issuer (lane 0 of warp 8): issues S_j = Q K_j^T (8 x tcgen05.mma kind::f16,
+//     M=N=K=128, operands in shared memory) into one of two TMEM S buffers, so the MMA of step
+//     j+1 runs while the rows are still in the softmax of step j, and PV_j as two K=64 halves,
+//     O_h += P_j[:, half h] V_j[half h, :], with P read from TMEM;
+//   - softmax (warps 0-7; a row = a TMEM lane, its 128 key columns split into two halves, one
+//     per warp): reads its half of S once with tcgen05.ld, masks keys past the row's position
+//     (only on tiles that reach it), keeps the half's own running max and sum in the exp2 domain
+//     (ex2.approx, one in four exponentials as a cubic on the FMA pipe), rescales the half's O
+//     in TMEM only when its max grows by more than 8 (a stale max is exact since 1/l uses the
 //     same max; a warp rescales together because tcgen05.ld/st are warp-collective), and writes
-//     P (bf16/fp16) in the canonical K-major 128B-swizzled layout;
-//   - mbarriers hand off K/V stages, S buffers, P and PV completion between the roles.
-// TMEM: two 128-column S buffers + a 128-column O accumulator (512 allocated; one CTA per SM by
-// its shared memory). Every wait is bounded in wall time and aborts the whole CTA through a
-// shared flag; an aborted CTA records bit 2 in *err, lets issued copies and MMAs land, frees its
-// TMEM and returns.
+//     P (bf16/fp16 pairs) with tcgen05.st over the S columns it has just read. The halves never
+//     wait for each other: they are merged once, in the epilogue, by their maxima;
+//   - mbarriers hand off K/V stages, S buffers, P and PV completion between the roles; QK(j+2)
+//     reuses S buffer j%2 after PV(j) has read the P in it.
+// TMEM: two 128-column S buffers + one 128-column O accumulator per key half (512 allocated; one
+// CTA per SM by its shared memory). Every wait is bounded in wall time and aborts the whole CTA
+// through a shared flag; an aborted CTA records bit 2 in *err, lets issued copies and MMAs land,
+// frees its TMEM and returns.
 #include <cuda.h>
 
 #include <mutex>
@@ -48,9 +50,9 @@ constexpr int kBlock = 16384;  // one 128 x 64 bf16 swizzled block
 constexpr int kSmem = 10 * kBlock + 1024 + 256;
 constexpr unsigned long long kWaitNs = 1000000000ull;  // 1 s: legitimate waits here take microseconds
 constexpr unsigned long long kAbortWaitNs = 20000000ull;  // 20 ms per barrier phase on the abort path
-// TMEM columns: S buffers 0-127 and 128-255 (fp32), O 256-383 (fp32), P buffers 384-447 and
-// 448-511 (bf16/fp16 pairs).
-constexpr uint32_t kTmemO = 256, kTmemP = 384;
+// TMEM columns: S buffers 0-127 and 128-255 (fp32; each column half also holds that half's P,
+// bf16/fp16 pairs, once read), O accumulators of key halves 0 and 1 at 256-383 and 384-511.
+constexpr uint32_t kTmemO = 256;
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
@@ -284,7 +286,7 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
   uint64_t* k_full = bars + 1;   // [2] K stage loaded
   uint64_t* v_full = bars + 3;   // [2] V stage loaded
   uint64_t* s_full = bars + 5;   // [2] S buffer written by QK
-  uint64_t* s_free = bars + 7;   // [2] S buffer read by the softmax
+  // bars 7-8: unused
   uint64_t* p_full = bars + 9;   // [2] P buffer written by the softmax
   uint64_t* pv_done = bars + 11; // [2] PV of P buffer b complete (buffer reusable, O stable)
   uint64_t* k_free = bars + 13;  // [2] K stage read by its QK
@@ -327,8 +329,6 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
     mbar_init(&v_full[1], 1);
     mbar_init(&s_full[0], 1);
     mbar_init(&s_full[1], 1);
-    mbar_init(&s_free[0], kSoftWarps * 32);
-    mbar_init(&s_free[1], kSoftWarps * 32);
     mbar_init(&p_full[0], kSoftWarps * 32);
     mbar_init(&p_full[1], kSoftWarps * 32);
     mbar_init(&pv_done[0], 1);
@@ -387,21 +387,24 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
       constexpr uint32_t idesc_pv = idesc_f16(fmt, 1, kRows, kD);
       const uint32_t aQ = smem_u32(sQ), aK = smem_u32(sK), aV = smem_u32(sV);
       // PV(j): O += P_j V_j, P_j from TMEM (P buffer j%2: 64 columns of packed 16-bit pairs)
+      // PV(j): O_h += P_j[:, keys of half h] V_j[keys of half h, :] for h = 0, 1; P of half h sits
+      // in S buffer j%2 at columns 64*h .. 64*h+31 (packed pairs)
       auto issue_pv = [&](int j) {
         const int b = j & 1;
         const uint32_t vbase = aV + b * 2 * kBlock;
 #pragma unroll
         for (int k = 0; k < kKeys / 16; ++k)
-          mma_f16_ts(tmem + kTmemO, tmem + kTmemP + b * (kKeys / 2) + k * 8,
-                     sw128_desc(vbase + k * 16 * 128, kBlock, 1024), idesc_pv, (j > 0 || k > 0) ? 1u : 0u);
+          mma_f16_ts(tmem + kTmemO + (k >> 2) * 128, tmem + b * kKeys + (k >> 2) * 64 + (k & 3) * 8,
+                     sw128_desc(vbase + k * 16 * 128, kBlock, 1024), idesc_pv, (j > 0 || (k & 3) > 0) ? 1u : 0u);
         mma_commit(&pv_done[b]);
         mma_commit(&v_free[b]);
       };
       bool ok = true;
       for (int j = 0; j < nsteps && ok; ++j) {
         const int s = j & 1;
+        // S buffer s holds P(j-2) until PV(j-2) has read it
         ok = wait(&k_full[s], (j >> 1) & 1) && (j > 0 || wait(q_full, 0)) &&
-             (j < 2 || wait(&s_free[s], ((j - 2) >> 1) & 1));
+             (j < 2 || wait(&pv_done[s], ((j - 2) >> 1) & 1));
         if (!ok) break;
         tc_fence_after();
         const uint32_t kbase = aK + s * 2 * kBlock;
@@ -429,10 +432,12 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
     }
   } else {
     // ------------------------------------------------------------------ softmax
+    // Each key half keeps its own running max, sum and O accumulator, so the two warps of a lane
+    // quadrant never wait for each other; the halves are merged once, in the epilogue.
     const uint32_t lane_off = (uint32_t)(quad * 32) << 16;
     const uint32_t col = part * kColsPerWarp;
-    const uint32_t tO = tmem + kTmemO + col;
-    float m = -INFINITY, l = 0.f;  // l: this part's share of the row sum
+    const uint32_t tOh = tmem + kTmemO + part * 128;  // this half's O accumulator
+    float m = -INFINITY, l = 0.f;
     bool ok = true;
     for (int j = 0; j < nsteps; ++j) {
       const int s = j & 1;
@@ -451,9 +456,6 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
 #pragma unroll
           for (int i = 0; i < 32; ++i) v[c * 32 + i] = __uint_as_float(r[c][i]);
       }
-      // S buffer s is in registers: QK(j+2) may overwrite it
-      tc_fence_before();
-      mbar_arrive(&s_free[s]);
       const long long key0 = (long long)j * kKeys + col;
       if (__any_sync(0xffffffffu, key0 + kColsPerWarp - 1 > p)) {
 #pragma unroll
@@ -463,51 +465,41 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
       float tmax = v[0];
 #pragma unroll
       for (int i = 1; i < kColsPerWarp; ++i) tmax = fmaxf(tmax, v[i]);
-      s_part[s][part][trow] = tmax * scale_log2;
-      quad_sync(quad);
-      float m_new = m;
-#pragma unroll
-      for (int q = 0; q < kWarpsPerQuad; ++q) m_new = fmaxf(m_new, s_part[s][q][trow]);
+      const float m_new = fmaxf(m, tmax * scale_log2);  // -inf while every key of this half is masked
       const bool rescale = j > 0 && m_new > m + 8.f;
       float alpha = 1.f;
       if (j == 0 || rescale) {
-        alpha = ex2(m - m_new);  // 0 for the first step
+        alpha = m == -INFINITY ? 0.f : ex2(m - m_new);
         l *= alpha;
         m = m_new;
       }
-      // P (this part's 64 keys, packed in pairs) in registers; one in four exponentials on the FMA pipe
+      const float mu = m == -INFINITY ? 0.f : m;  // all-masked half: exponentials of -inf give 0
       uint32_t pk[kColsPerWarp / 2];
 #pragma unroll
       for (int i = 0; i < kColsPerWarp; i += 2) {
-        const float p0 = ex2(fmaf(v[i], scale_log2, -m));
-        const float x1 = fmaf(v[i + 1], scale_log2, -m);
+        const float p0 = ex2(fmaf(v[i], scale_log2, -mu));
+        const float x1 = fmaf(v[i + 1], scale_log2, -mu);
         const float p1 = ((i >> 1) & 1) ? ex2_poly(x1) : ex2(x1);
         l += p0 + p1;
         pk[i / 2] = pack2<T>(p0, p1);
       }
-      // P buffer s was last read by PV(j-2)
-      if (j >= 2) {
-        ok = __all_sync(0xffffffffu, wait(&pv_done[s], ((j - 2) >> 1) & 1));
-        if (!ok) break;
-      }
-      // O must be stable (PV(j-1) complete) to rescale it; tcgen05.ld/st are warp-collective, so
-      // the warp rescales together, other lanes by 1
+      // this half's O must be stable (PV(j-1) complete) to rescale it; tcgen05.ld/st are
+      // warp-collective, so the warp rescales together, other lanes by 1
       if (__any_sync(0xffffffffu, rescale)) {
         ok = __all_sync(0xffffffffu, wait(&pv_done[s ^ 1], ((j - 1) >> 1) & 1));
         if (!ok) break;
         tc_fence_after();
 #pragma unroll 1
-        for (int c = 0; c < kColsPerWarp / 32; ++c) {
+        for (int c = 0; c < kD / 32; ++c) {
           float o[32];
-          tmem_ld32(tO + lane_off + c * 32, o);
+          tmem_ld32(tOh + lane_off + c * 32, o);
 #pragma unroll
           for (int i = 0; i < 32; ++i) o[i] *= alpha;
-          tmem_st32(tO + lane_off + c * 32, o);
+          tmem_st32(tOh + lane_off + c * 32, o);
         }
-      } else if (j >= 2) {
-        tc_fence_after();
       }
-      tmem_st32u(tmem + kTmemP + s * (kKeys / 2) + part * (kColsPerWarp / 2) + lane_off, pk);
+      // P over this warp's own S columns (already in registers): QK(j+2) waits for PV(j)
+      tmem_st32u(tmem + s * kKeys + part * 64 + lane_off, pk);
       asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
       tc_fence_before();
       mbar_arrive(&p_full[s]);
@@ -515,22 +507,29 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
     if (ok) ok = __all_sync(0xffffffffu, wait(&pv_done[(nsteps - 1) & 1], ((nsteps - 1) >> 1) & 1));
     if (ok) {
       tc_fence_after();
-      s_part[0][part][trow] = l;
+      // merge the halves: O = (O_0 2^(m_0 - M) + O_1 2^(m_1 - M)) / (l_0 2^(m_0 - M) + l_1 2^(m_1 - M))
+      s_part[0][part][trow] = m;
+      s_part[1][part][trow] = l;
       quad_sync(quad);
-      float lsum = 0.f;
-#pragma unroll
-      for (int q = 0; q < kWarpsPerQuad; ++q) lsum += s_part[0][q][trow];
-      const float inv = 1.f / lsum;
+      const float m0 = s_part[0][0][trow], m1 = s_part[0][1][trow];
+      const float M = fmaxf(m0, m1);  // finite: key 0 is in half 0 and visible to every row
+      const float a0 = m0 == -INFINITY ? 0.f : ex2(m0 - M), a1 = m1 == -INFINITY ? 0.f : ex2(m1 - M);
+      const float inv = 1.f / (s_part[1][0][trow] * a0 + s_part[1][1][trow] * a1);
+      const float c0 = a0 * inv, c1 = a1 * inv;
       T* orow = out + ((long long)row * Hq + h) * kD + col;
 #pragma unroll 1
       for (int c = 0; c < kColsPerWarp / 32; ++c) {
-        float o[32];
-        tmem_ld32(tO + lane_off + c * 32, o);
+        float o0[32], o1[32];
+        tmem_ld32(tmem + kTmemO + col + lane_off + c * 32, o0);
+        tmem_ld32(tmem + kTmemO + 128 + col + lane_off + c * 32, o1);
         if (live) {
 #pragma unroll
           for (int i = 0; i < 32; i += 8) {
-            uint4 w = make_uint4(pack2<T>(o[i] * inv, o[i + 1] * inv), pack2<T>(o[i + 2] * inv, o[i + 3] * inv),
-                                 pack2<T>(o[i + 4] * inv, o[i + 5] * inv), pack2<T>(o[i + 6] * inv, o[i + 7] * inv));
+            float w8[8];
+#pragma unroll
+            for (int e = 0; e < 8; ++e) w8[e] = fmaf(o0[i + e], c0, o1[i + e] * c1);
+            uint4 w = make_uint4(pack2<T>(w8[0], w8[1]), pack2<T>(w8[2], w8[3]), pack2<T>(w8[4], w8[5]),
+                                 pack2<T>(w8[6], w8[7]));
             *reinterpret_cast<uint4*>(orow + c * 32 + i) = w;
           }
         }
