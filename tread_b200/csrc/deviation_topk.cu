@@ -47,6 +47,33 @@ __device__ __forceinline__ void load_row(const T* p, float (&x)[E]) {
   }
 }
 
+// A lane's E elements of a row, kept as the loaded bytes until they are used: rows of several
+// heads can then be in flight at once within the register budget (bf16 E = 4: 2 registers).
+template <typename T, int E>
+struct RawRow {
+  static constexpr int kWords = (E * (int)sizeof(T) + 3) / 4;
+  uint32_t w[kWords];
+  __device__ __forceinline__ void load(const T* p) {
+    if constexpr (kWords == 4) {
+      const uint4 v = __ldg(reinterpret_cast<const uint4*>(p));
+      w[0] = v.x; w[1] = v.y; w[2] = v.z; w[3] = v.w;
+    } else if constexpr (kWords == 2) {
+      const uint2 v = __ldg(reinterpret_cast<const uint2*>(p));
+      w[0] = v.x; w[1] = v.y;
+    } else if constexpr (kWords == 1) {
+      w[0] = __ldg(reinterpret_cast<const unsigned*>(p));
+    } else {
+#pragma unroll
+      for (int i = 0; i < kWords; ++i) w[i] = __ldg(reinterpret_cast<const unsigned*>(p) + i);
+    }
+  }
+  __device__ __forceinline__ void to_float(float (&x)[E]) const {
+    const T* e = reinterpret_cast<const T*>(w);
+#pragma unroll
+    for (int i = 0; i < E; ++i) x[i] = Num<T>::to_f(e[i]);
+  }
+};
+
 template <int E>
 __device__ __forceinline__ float row_norm(const float (&a)[E], const float (&b)[E]) {
   float p = 0.f;
@@ -327,40 +354,51 @@ __global__ void __launch_bounds__(kThreads, 2)
                           float* __restrict__ dev_out, int64_t* __restrict__ sel_idx, int64_t* __restrict__ sel_pos,
                           unsigned* __restrict__ workspace) {
   const int lane = threadIdx.x & 31;
-  for (int t = blockIdx.x * kWarps + (threadIdx.x >> 5); t < n; t += gridDim.x * kWarps) {
-    const long long pos = cand_pos[t];
+  const int stride = gridDim.x * kWarps;
+  int t = blockIdx.x * kWarps + (threadIdx.x >> 5);
+  long long pos = t < n ? cand_pos[t] : 0;
+  for (; t < n; t += stride) {
+    // the next candidate's position loads while this one's rows do
+    const long long pos_next = t + stride < n ? cand_pos[t + stride] : 0;
     float dev;
     if (pos < 0 || pos >= T_cache) {
       if (lane == 0) atomicOr(workspace + 1, 1u);  // sticky error flag for the caller
       dev = __int_as_float(0x7fc00000);
     } else {
       float a = 0.f, b = 0.f;
-      constexpr int HU = E <= 4 ? 2 : 1;  // heads whose rows are in flight together
+      // heads whose rows are in flight together (raw bytes: 8 x HU registers for bf16 D = 128)
+      constexpr int HU = RawRow<T, E>::kWords <= 2 ? 4 : (RawRow<T, E>::kWords <= 4 ? 2 : 1);
 #pragma unroll 1
       for (int h0 = 0; h0 < H; h0 += HU) {
-        float fk[HU][E], ck[HU][E], fv[HU][E], cv[HU][E];
+        RawRow<T, E> fk[HU], ck[HU], fv[HU], cv[HU];
 #pragma unroll
         for (int j = 0; j < HU; ++j) {
           if (h0 + j < H) {
             const long long fo = (long long)t * f_st + (long long)(h0 + j) * f_sh + lane * E;
             const long long co = pos * c_st + (long long)(h0 + j) * c_sh + lane * E;
-            load_row<T, E>(k1 + fo, fk[j]);
-            load_row<T, E>(K1 + co, ck[j]);
-            load_row<T, E>(v1 + fo, fv[j]);
-            load_row<T, E>(V1 + co, cv[j]);
+            fk[j].load(k1 + fo);
+            ck[j].load(K1 + co);
+            fv[j].load(v1 + fo);
+            cv[j].load(V1 + co);
           }
         }
 #pragma unroll
         for (int j = 0; j < HU; ++j) {
           if (h0 + j < H) {
-            a = __fadd_rn(a, row_norm<E>(fk[j], ck[j]));
-            b = __fadd_rn(b, row_norm<E>(fv[j], cv[j]));
+            float x[E], y[E];
+            fk[j].to_float(x);
+            ck[j].to_float(y);
+            a = __fadd_rn(a, row_norm<E>(x, y));
+            fv[j].to_float(x);
+            cv[j].to_float(y);
+            b = __fadd_rn(b, row_norm<E>(x, y));
           }
         }
       }
       dev = __fadd_rn(a, b);
     }
     if (lane == 0) dev_out[t] = dev;
+    pos = pos_next;
   }
   if (budget <= 0) return;
   __shared__ bool s_last;
