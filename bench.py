@@ -62,7 +62,7 @@ def parse():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=10.0, help="CPU baseline sample budget")
     ap.add_argument("--no-ttft", action="store_true", help="skip the configs[2] 7B TTFT leg")
-    ap.add_argument("--only", choices=["attention", "selector"], default=None,
+    ap.add_argument("--only", choices=["attention", "selector", "ttft"], default=None,
                     help="run one kernel microbench alone (for profiler captures) and print its timing")
     ap.add_argument("--ttft-reps", type=int, default=5, help="timed warm requests per recompute ratio")
     ap.add_argument("--no-dp", action="store_true", help="skip the configs[4] hash-sharded replica serving leg")
@@ -761,10 +761,44 @@ def run_e2e(args, dev, pool_k, pool_v, ids, deltas, inv, world, rank):
             "path": "pinned host blocks -> tread_kv_fetch -> tread_rope_gather_append -> tread_kv_spill_rows"}
 
 
+def run_only_ttft(args):
+    """One configs[2] request at 20% recompute (eager), after a cold pass and --warmup warm requests,
+    bracketed by cudaProfilerStart/Stop so that a profiler started with --profile-from-start off
+    sees exactly that request's launches."""
+    from tread_b200 import BlockStore, Engine
+    from tread_b200.configs import random_model, random_tokens
+
+    dev = torch.device("cuda", 0)
+    model = random_model("qwen2.5-7b", dtype=torch.bfloat16, device=dev, seed=args.seed, init_on_device=True)
+    V = model.config.vocab_size
+    g = torch.Generator().manual_seed(args.seed + 3)
+    prefix = random_tokens(256, V, g)
+    docs = [random_tokens(496, V, g) for _ in range(16)]
+    query = random_tokens(64, V, g)
+    eng = Engine(model, BlockStore(64 << 30))
+    eng.prefill(prefix, docs, query)
+    pg = torch.Generator().manual_seed(args.seed + 5)
+    for _ in range(max(1, args.warmup)):
+        eng.prefill(prefix, [docs[i] for i in torch.randperm(16, generator=pg).tolist()], query, ratio=0.2)
+    order = [docs[i] for i in torch.randperm(16, generator=pg).tolist()]
+    torch.cuda.synchronize(dev)
+    torch.cuda.cudart().cudaProfilerStart()
+    t0 = time.perf_counter()
+    logits, _, st = eng.prefill(prefix, order, query, ratio=0.2)
+    int(logits.argmax().item())
+    t1 = time.perf_counter()
+    torch.cuda.cudart().cudaProfilerStop()
+    print(json.dumps({"only": "ttft", "ttft_ms": round((t1 - t0) * 1e3, 2),
+                      "stages_ms": {k: round(v * 1e3, 2) for k, v in st.t.items()}}), flush=True)
+    return 0
+
+
 def run_only(args):
     """One kernel alone on configs[2]/[1] shapes, --warmup + --steps launches (profiler captures)."""
     from tread_b200 import kernels
 
+    if args.only == "ttft":
+        return run_only_ttft(args)
     dev = torch.device("cuda", 0)
     gen = torch.Generator(device=dev).manual_seed(args.seed)
     T_ctx, nq, Hq = 16 * 496 + 256, 64, 28
