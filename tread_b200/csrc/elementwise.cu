@@ -5,8 +5,10 @@
 // mul, cast, mul) and 2 for the activation (silu, mul), each a full pass over HBM. Here each is
 // one pass with the same rounding points as HF's modules:
 //   rmsnorm : y = to_dtype( w * to_dtype( x * rsqrt(mean(x^2) + eps) ) )   (x in fp32)
-//   silu_mul: y = to_dtype( to_dtype(silu(g)) * u ),  silu(g) = g / (1 + exp(-g)) in fp32
+//   silu_mul: y = to_dtype( to_dtype(silu(g)) * u ),  silu(g) = g / (1 + exp(-g)) in fp32 (for
+//             16-bit types with the fast exponential and division intrinsics)
 #include <algorithm>
+#include <type_traits>
 
 #include "common.cuh"
 
@@ -59,26 +61,48 @@ __global__ void __launch_bounds__(kNormThreads)
   }
 }
 
+constexpr int kSiluThreads = 256;
+constexpr int kSiluUnroll = 2;  // 16-byte vectors of gate and of up in flight per thread
+
+// One CTA per row (no index division), kSiluUnroll vectors per thread per iteration.
 template <typename T>
-__global__ void silu_mul_kernel(const T* __restrict__ gu, long long ld, T* __restrict__ y, long long ldy, int I,
-                                long long rows) {
+__global__ void __launch_bounds__(kSiluThreads)
+    silu_mul_kernel(const T* __restrict__ gu, long long ld, T* __restrict__ y, long long ldy, int I) {
   constexpr int VEC = 16 / sizeof(T);
   const int vpr = I / VEC;
-  const long long total = rows * vpr;
-  for (long long t = blockIdx.x * (long long)blockDim.x + threadIdx.x; t < total;
-       t += (long long)gridDim.x * blockDim.x) {
-    const long long r = t / vpr;
-    const int v = (int)(t - r * vpr);
-    Vec16<T> g, u, o;
-    g.raw = __ldg(reinterpret_cast<const int4*>(gu + r * ld) + v);
-    u.raw = __ldg(reinterpret_cast<const int4*>(gu + r * ld + I) + v);
+  const long long r = blockIdx.x;
+  const int4* g = reinterpret_cast<const int4*>(gu + r * ld);
+  const int4* u = reinterpret_cast<const int4*>(gu + r * ld + I);
+  int4* o = reinterpret_cast<int4*>(y + r * ldy);
+  for (int v0 = threadIdx.x; v0 < vpr; v0 += kSiluThreads * kSiluUnroll) {
+    Vec16<T> gv[kSiluUnroll], uv[kSiluUnroll];
 #pragma unroll
-    for (int e = 0; e < VEC; ++e) {
-      const float gf = Num<T>::to_f(g.e[e]);
-      const float s = Num<T>::to_f(Num<T>::from_f(gf / (1.f + expf(-gf))));
-      o.e[e] = Num<T>::from_f(s * Num<T>::to_f(u.e[e]));
+    for (int k = 0; k < kSiluUnroll; ++k) {
+      const int v = v0 + k * kSiluThreads;
+      if (v < vpr) {
+        gv[k].raw = __ldg(g + v);
+        uv[k].raw = __ldg(u + v);
+      }
     }
-    reinterpret_cast<int4*>(y + r * ldy)[v] = o.raw;
+#pragma unroll
+    for (int k = 0; k < kSiluUnroll; ++k) {
+      const int v = v0 + k * kSiluThreads;
+      if (v < vpr) {
+        Vec16<T> ov;
+#pragma unroll
+        for (int e = 0; e < VEC; ++e) {
+          const float gf = Num<T>::to_f(gv[k].e[e]);
+          // 16-bit outputs: the fast exponential / division differ from the exact ones by ~1e-6
+          // relative, which moves the 16-bit rounding of silu(g) by at most one unit, rarely;
+          // fp32 keeps the exact functions
+          const float sg = std::is_same<T, float>::value ? gf / (1.f + expf(-gf))
+                                                         : __fdividef(gf, 1.f + __expf(-gf));
+          const float sv = Num<T>::to_f(Num<T>::from_f(sg));
+          ov.e[e] = Num<T>::from_f(sv * Num<T>::to_f(uv[k].e[e]));
+        }
+        o[v] = ov.raw;
+      }
+    }
   }
 }
 
@@ -132,21 +156,21 @@ extern "C" int tread_silu_mul(const void* gate_up, int64_t ld_gu, void* y, int64
                       (ld_gu * es) % 16 == 0 && (ld_y * es) % 16 == 0,
                   "silu_mul: inter/ld must be multiples of 16 bytes");
   TREAD_CHECK_ARG(al16(gate_up) && al16(y), "silu_mul: pointers not 16-byte aligned");
+  TREAD_CHECK_ARG(rows < (1LL << 31), "silu_mul: rows >= 2^31");
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
-  const long long vecs = rows * (long long)(inter * es / 16);
-  const unsigned grid = (unsigned)std::min<long long>((vecs + 255) / 256, 148LL * 16);
+  const unsigned grid = (unsigned)rows;
   switch (dtype) {
     case TREAD_BF16:
-      silu_mul_kernel<__nv_bfloat16><<<grid, 256, 0, st>>>(static_cast<const __nv_bfloat16*>(gate_up), ld_gu,
-                                                           static_cast<__nv_bfloat16*>(y), ld_y, inter, rows);
+      silu_mul_kernel<__nv_bfloat16><<<grid, kSiluThreads, 0, st>>>(
+          static_cast<const __nv_bfloat16*>(gate_up), ld_gu, static_cast<__nv_bfloat16*>(y), ld_y, inter);
       break;
     case TREAD_F16:
-      silu_mul_kernel<__half><<<grid, 256, 0, st>>>(static_cast<const __half*>(gate_up), ld_gu,
-                                                    static_cast<__half*>(y), ld_y, inter, rows);
+      silu_mul_kernel<__half><<<grid, kSiluThreads, 0, st>>>(static_cast<const __half*>(gate_up), ld_gu,
+                                                            static_cast<__half*>(y), ld_y, inter);
       break;
     default:
-      silu_mul_kernel<float><<<grid, 256, 0, st>>>(static_cast<const float*>(gate_up), ld_gu, static_cast<float*>(y),
-                                                   ld_y, inter, rows);
+      silu_mul_kernel<float><<<grid, kSiluThreads, 0, st>>>(static_cast<const float*>(gate_up), ld_gu,
+                                                           static_cast<float*>(y), ld_y, inter);
       break;
   }
   TREAD_CHECK_LAUNCH("silu_mul_kernel");

@@ -25,7 +25,8 @@ template <typename T>
 __global__ void __launch_bounds__(kThreads)
     rope_rows_kernel(const T* __restrict__ qkv, long long ld, const int64_t* __restrict__ pos, int Hq, int Hkv,
                      int D, T* __restrict__ q_out, T* __restrict__ Kc, T* __restrict__ Vc, long long c_sh,
-                     long long T_cache, int kv_by_row, const __grid_constant__ Freq f, float scale, unsigned* err) {
+                     long long T_cache, int kv_by_row, const __grid_constant__ Freq f, float scale, unsigned* err,
+                     int vec) {
   __shared__ float s_cos[kMaxHalf], s_sin[kMaxHalf];
   const int r = blockIdx.x;
   const long long p = pos[r];
@@ -44,6 +45,36 @@ __global__ void __launch_bounds__(kThreads)
   __syncthreads();
   const T* row = qkv + (long long)r * ld;
   const int q0 = q_out ? 0 : Hq;  // no q output: rotate the k heads only
+  if (vec) {
+    // 16-byte vectors: VEC consecutive pairs (i, i + D/2) of one head per step, same fp32 math
+    constexpr int VEC = 16 / sizeof(T);
+    const int hv = half / VEC;
+    const int nvec = (Hq + Hkv - q0) * hv;
+    for (int w = threadIdx.x; w < nvec; w += kThreads) {
+      const int head = q0 + w / hv, i0 = (w % hv) * VEC;
+      const T* src = row + head * D + i0;
+      Vec16<T> a, b, oa, ob;
+      a.raw = __ldg(reinterpret_cast<const int4*>(src));
+      b.raw = __ldg(reinterpret_cast<const int4*>(src + half));
+#pragma unroll
+      for (int e = 0; e < VEC; ++e) {
+        const float x1 = Num<T>::to_f(a.e[e]), x2 = Num<T>::to_f(b.e[e]);
+        oa.e[e] = Num<T>::from_f(__fsub_rn(__fmul_rn(x1, s_cos[i0 + e]), __fmul_rn(x2, s_sin[i0 + e])));
+        ob.e[e] = Num<T>::from_f(__fadd_rn(__fmul_rn(x2, s_cos[i0 + e]), __fmul_rn(x1, s_sin[i0 + e])));
+      }
+      T* dst = head < Hq ? q_out + ((long long)r * Hq + head) * D : Kc + (head - Hq) * c_sh + slot * D;
+      *reinterpret_cast<int4*>(dst + i0) = oa.raw;
+      *reinterpret_cast<int4*>(dst + i0 + half) = ob.raw;
+    }
+    const T* vsrc = row + (Hq + Hkv) * D;
+    const int vpd = D / VEC;
+    for (int w = threadIdx.x; w < Hkv * vpd; w += kThreads) {
+      const int g = w / vpd, d = (w - g * vpd) * VEC;
+      *reinterpret_cast<int4*>(Vc + g * c_sh + slot * D + d) =
+          __ldg(reinterpret_cast<const int4*>(vsrc + g * D + d));
+    }
+    return;
+  }
   const int nrot = (Hq + Hkv - q0) * half;  // rotation pairs over q heads then k heads
   for (int w = threadIdx.x; w < nrot; w += kThreads) {
     const int head = q0 + w / half, i = w % half;
@@ -83,24 +114,29 @@ extern "C" int tread_rope_rows(const void* qkv, int64_t ld_qkv, const int64_t* p
   for (int i = 0; i < D / 2; ++i) f.inv[i] = inv_freq[i];
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
   unsigned* err = static_cast<unsigned*>(err_flag);
+  // 16-byte vector path when every row, head half and cache slot starts on a 16-byte boundary
+  const int64_t vec_el = 16 / (int64_t)dtype_size(dtype);
+  auto al16 = [](const void* p) { return p == nullptr || (reinterpret_cast<uintptr_t>(p) & 15u) == 0; };
+  const int vec = (D / 2) % vec_el == 0 && ld_qkv % vec_el == 0 && cache_stride_head % vec_el == 0 && al16(qkv) &&
+                  al16(q_out) && al16(K_cache) && al16(V_cache);
   switch (dtype) {
     case TREAD_BF16:
       rope_rows_kernel<__nv_bfloat16><<<R, kThreads, 0, st>>>(
           static_cast<const __nv_bfloat16*>(qkv), ld_qkv, pos, Hq, Hkv, D, static_cast<__nv_bfloat16*>(q_out),
           static_cast<__nv_bfloat16*>(K_cache), static_cast<__nv_bfloat16*>(V_cache), cache_stride_head, T_cache, kv_by_row, f,
-          attn_scaling, err);
+          attn_scaling, err, vec);
       break;
     case TREAD_F16:
       rope_rows_kernel<__half><<<R, kThreads, 0, st>>>(
           static_cast<const __half*>(qkv), ld_qkv, pos, Hq, Hkv, D, static_cast<__half*>(q_out),
           static_cast<__half*>(K_cache), static_cast<__half*>(V_cache), cache_stride_head, T_cache, kv_by_row, f, attn_scaling,
-          err);
+          err, vec);
       break;
     default:
       rope_rows_kernel<float><<<R, kThreads, 0, st>>>(
           static_cast<const float*>(qkv), ld_qkv, pos, Hq, Hkv, D, static_cast<float*>(q_out),
           static_cast<float*>(K_cache), static_cast<float*>(V_cache), cache_stride_head, T_cache, kv_by_row, f, attn_scaling,
-          err);
+          err, vec);
       break;
   }
   TREAD_CHECK_LAUNCH("rope_rows_kernel");
