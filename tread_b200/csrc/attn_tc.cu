@@ -17,7 +17,7 @@
 //   - softmax (warps 0-7; a row = a TMEM lane, its 128 key columns split into two halves, one
 //     per warp): reads its half of S once with tcgen05.ld, masks keys past the row's position
 //     (only on tiles that reach it), keeps the half's own running max and sum in the exp2 domain
-//     (ex2.approx, one in four exponentials as a cubic on the FMA pipe), rescales the half's O
+//     (ex2.approx on the MUFU pipe, which stays below saturation), rescales the half's O
 //     in TMEM only when its max grows by more than 8 (a stale max is exact since 1/l uses the
 //     same max; a warp rescales together because tcgen05.ld/st are warp-collective), and writes
 //     P (bf16/fp16 pairs) with tcgen05.st over the S columns it has just read. The halves never
@@ -256,20 +256,6 @@ __device__ __forceinline__ float ex2(float x) {
   return y;
 }
 
-// 2^x on the FMA pipe, to take a quarter of the exponentials off the MUFU pipe (which otherwise
-// needs as many cycles per step as the tensor core): x = i + f with i = round(x) by the
-// 1.5 * 2^23 addition (FADDs only), 2^f on [-0.5, 0.5] from a cubic fitted here (iteratively
-// reweighted least squares on Chebyshev nodes, relative error) with max relative error 7.5e-5,
-// far below the rounding of P to bf16/fp16; 2^i is added to the exponent bits. Arguments below
-// -126 give 2^-126-scale values (probabilities that vanish next to the row maximum's 1).
-__device__ __forceinline__ float ex2_poly(float x) {
-  x = fmaxf(x, -126.f);
-  const float t = __fadd_rn(x, 12582912.f);
-  const float f = __fsub_rn(x, __fsub_rn(t, 12582912.f));
-  const float p = fmaf(fmaf(fmaf(0.055171654f, f, 0.24261113f), f, 0.69326097f), f, 0.99992806f);
-  return __int_as_float(__float_as_int(p) + (__float_as_int(t) << 23));
-}
-
 template <typename T>
 __global__ void __launch_bounds__(kThreadsTC, 1)
     attn_rows_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
@@ -478,8 +464,7 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
 #pragma unroll
       for (int i = 0; i < kColsPerWarp; i += 2) {
         const float p0 = ex2(fmaf(v[i], scale_log2, -mu));
-        const float x1 = fmaf(v[i + 1], scale_log2, -mu);
-        const float p1 = ((i >> 1) & 1) ? ex2_poly(x1) : ex2(x1);
+        const float p1 = ex2(fmaf(v[i + 1], scale_log2, -mu));
         l += p0 + p1;
         pk[i / 2] = pack2<T>(p0, p1);
       }
