@@ -256,6 +256,34 @@ __device__ __forceinline__ float ex2(float x) {
   return y;
 }
 
+// Packed two-wide fp32 arithmetic of sm_100 (one issue slot for two lanes' worth of work): the
+// softmax is issue-bound, so halving its FMAs and adds shortens each step.
+__device__ __forceinline__ float2 ffma2(float2 a, float2 b, float2 c) {
+  float2 d;
+  asm("{\n\t.reg .b64 ra, rb, rc, rd;\n\t"
+      "mov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\tmov.b64 rc, {%6, %7};\n\t"
+      "fma.rn.f32x2 rd, ra, rb, rc;\n\tmov.b64 {%0, %1}, rd;\n\t}"
+      : "=f"(d.x), "=f"(d.y)
+      : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y), "f"(c.x), "f"(c.y));
+  return d;
+}
+
+__device__ __forceinline__ float2 fadd2(float2 a, float2 b) {
+  float2 d;
+  asm("{\n\t.reg .b64 ra, rb, rd;\n\t"
+      "mov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\t"
+      "add.rn.f32x2 rd, ra, rb;\n\tmov.b64 {%0, %1}, rd;\n\t}"
+      : "=f"(d.x), "=f"(d.y)
+      : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y));
+  return d;
+}
+
+__device__ __forceinline__ float fmax3(float a, float b, float c) {
+  float d;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+  return d;
+}
+
 template <typename T>
 __global__ void __launch_bounds__(kThreadsTC, 1)
     attn_rows_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
@@ -448,9 +476,10 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
         for (int i = 0; i < kColsPerWarp; ++i)
           if (key0 + i > p) v[i] = -INFINITY;
       }
-      float tmax = v[0];
+      float m4[4] = {v[0], v[1], v[2], v[3]};  // four independent 3-input max chains
 #pragma unroll
-      for (int i = 1; i < kColsPerWarp; ++i) tmax = fmaxf(tmax, v[i]);
+      for (int i = 4; i < kColsPerWarp; i += 2) m4[(i >> 1) & 3] = fmax3(m4[(i >> 1) & 3], v[i], v[i + 1]);
+      const float tmax = fmax3(m4[0], m4[1], fmaxf(m4[2], m4[3]));
       const float m_new = fmaxf(m, tmax * scale_log2);  // -inf while every key of this half is masked
       const bool rescale = j > 0 && m_new > m + 8.f;
       float alpha = 1.f;
@@ -461,13 +490,16 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
       }
       const float mu = m == -INFINITY ? 0.f : m;  // all-masked half: exponentials of -inf give 0
       uint32_t pk[kColsPerWarp / 2];
+      const float2 sc2 = make_float2(scale_log2, scale_log2), nm2 = make_float2(-mu, -mu);
+      float2 l2 = make_float2(0.f, 0.f);  // even / odd key sums
 #pragma unroll
       for (int i = 0; i < kColsPerWarp; i += 2) {
-        const float p0 = ex2(fmaf(v[i], scale_log2, -mu));
-        const float p1 = ex2(fmaf(v[i + 1], scale_log2, -mu));
-        l += p0 + p1;
-        pk[i / 2] = pack2<T>(p0, p1);
+        const float2 x = ffma2(make_float2(v[i], v[i + 1]), sc2, nm2);
+        const float2 pp = make_float2(ex2(x.x), ex2(x.y));
+        l2 = fadd2(l2, pp);
+        pk[i / 2] = pack2<T>(pp.x, pp.y);
       }
+      l += l2.x + l2.y;
       // this half's O must be stable (PV(j-1) complete) to rescale it; tcgen05.ld/st are
       // warp-collective, so the warp rescales together, other lanes by 1
       if (__any_sync(0xffffffffu, rescale)) {
