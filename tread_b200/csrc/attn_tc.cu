@@ -359,6 +359,8 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
   tc_fence_after();
   const uint32_t tmem = *s_tmem;
   const int nsteps = max(max(s_wmax[0], s_wmax[1]), max(s_wmax[2], s_wmax[3])) / kKeys + 1;
+  // padding rows past R (output discarded) see every key, so they never take the masking path
+  if (soft && row >= R) p = (long long)nsteps * kKeys - 1;
   const Waiter wait{s_abort};
 
   if (warp == kLoadWarp) {
@@ -472,9 +474,11 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
       }
       const long long key0 = (long long)j * kKeys + col;
       if (__any_sync(0xffffffffu, key0 + kColsPerWarp - 1 > p)) {
+        // keys i > lim of this half are past the row's position (one 32-bit compare each)
+        const int lim = (int)max(-1LL, min((long long)kColsPerWarp, p - key0));
 #pragma unroll
         for (int i = 0; i < kColsPerWarp; ++i)
-          if (key0 + i > p) v[i] = -INFINITY;
+          if (i > lim) v[i] = -INFINITY;
       }
       float m4[4] = {v[0], v[1], v[2], v[3]};  // four independent 3-input max chains
 #pragma unroll
