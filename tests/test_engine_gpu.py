@@ -306,7 +306,9 @@ def _sdpa_ref(q, K, V, pos):
 
 
 @pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
-@pytest.mark.parametrize("R,Hq,Hkv,T", [(17, 7, 1, 150), (300, 14, 2, 1000), (1651, 28, 4, 8256), (129, 8, 8, 129)])
+# the 4096-row case fills more than four waves of 148 SMs (896 tiles)
+@pytest.mark.parametrize("R,Hq,Hkv,T", [(17, 7, 1, 150), (300, 14, 2, 1000), (1651, 28, 4, 8256), (129, 8, 8, 129),
+                                        (4096, 28, 4, 4200)])
 def test_tensor_core_attention_matches_fp32_reference(cuda, dtype, R, Hq, Hkv, T):
     gen = torch.Generator(device=cuda).manual_seed(R + T)
     D = 128
