@@ -66,7 +66,7 @@ def parse():
                     help="run one kernel microbench alone (for profiler captures) and print its timing")
     ap.add_argument("--ttft-reps", type=int, default=5, help="timed warm requests per recompute ratio")
     ap.add_argument("--no-dp", action="store_true", help="skip the configs[4] hash-sharded replica serving leg")
-    ap.add_argument("--dp-rounds", type=int, default=12, help="timed serving rounds (one request per replica each)")
+    ap.add_argument("--dp-rounds", type=int, default=30, help="timed serving rounds (one request per replica each)")
     ap.add_argument("--no-tp", action="store_true",
                     help="skip the KV-head tensor-parallel TTFT legs (configs[2] 7B, configs[3] 32B)")
     return ap.parse_args()
@@ -561,7 +561,7 @@ def run_serving_dp(args, dev, world, rank):
         idx = torch.multinomial(w, k, replacement=False, generator=rg)
         return [pool[i] for i in idx.tolist()], random_tokens(64, V, rg)
 
-    warm = 6
+    warm = 10
     ttft, st_all = [], []
     s0 = None
     for rnd in range(warm + args.dp_rounds):
