@@ -17,7 +17,11 @@ namespace {
 
 constexpr int kNormThreads = 256;
 
-template <typename T>
+constexpr int kNormCache = 4;  // 16-byte vectors of the row a thread keeps in registers
+
+// CACHED: the row (<= kNormThreads * kNormCache vectors) is read from memory once and kept in
+// registers for the normalisation; otherwise it is read twice. Same arithmetic either way.
+template <typename T, bool CACHED>
 __global__ void __launch_bounds__(kNormThreads)
     rmsnorm_kernel(const T* __restrict__ x, long long ldx, const T* __restrict__ w, T* __restrict__ y,
                    long long ldy, int H, float eps) {
@@ -26,13 +30,32 @@ __global__ void __launch_bounds__(kNormThreads)
   T* yr = y + (long long)blockIdx.x * ldy;
   const int nvec = H / VEC;
   float ss = 0.f;
-  for (int i = threadIdx.x; i < nvec; i += kNormThreads) {
-    Vec16<T> a;
-    a.raw = __ldg(reinterpret_cast<const int4*>(xr) + i);
+  Vec16<T> xc[CACHED ? kNormCache : 1];
+  if constexpr (CACHED) {
 #pragma unroll
-    for (int e = 0; e < VEC; ++e) {
-      const float f = Num<T>::to_f(a.e[e]);
-      ss = fmaf(f, f, ss);
+    for (int k = 0; k < kNormCache; ++k) {
+      const int i = threadIdx.x + k * kNormThreads;
+      if (i < nvec) xc[k].raw = __ldg(reinterpret_cast<const int4*>(xr) + i);
+    }
+#pragma unroll
+    for (int k = 0; k < kNormCache; ++k) {
+      if (threadIdx.x + k * kNormThreads < nvec) {
+#pragma unroll
+        for (int e = 0; e < VEC; ++e) {
+          const float f = Num<T>::to_f(xc[k].e[e]);
+          ss = fmaf(f, f, ss);
+        }
+      }
+    }
+  } else {
+    for (int i = threadIdx.x; i < nvec; i += kNormThreads) {
+      Vec16<T> a;
+      a.raw = __ldg(reinterpret_cast<const int4*>(xr) + i);
+#pragma unroll
+      for (int e = 0; e < VEC; ++e) {
+        const float f = Num<T>::to_f(a.e[e]);
+        ss = fmaf(f, f, ss);
+      }
     }
   }
   __shared__ float s_red[kNormThreads / 32];
@@ -48,9 +71,8 @@ __global__ void __launch_bounds__(kNormThreads)
   }
   __syncthreads();
   const float r = rsqrtf(s_red[0] / (float)H + eps);
-  for (int i = threadIdx.x; i < nvec; i += kNormThreads) {
-    Vec16<T> a, b, o;
-    a.raw = __ldg(reinterpret_cast<const int4*>(xr) + i);
+  auto norm_store = [&](int i, const Vec16<T>& a) {
+    Vec16<T> b, o;
     b.raw = __ldg(reinterpret_cast<const int4*>(w) + i);
 #pragma unroll
     for (int e = 0; e < VEC; ++e) {
@@ -58,6 +80,19 @@ __global__ void __launch_bounds__(kNormThreads)
       o.e[e] = Num<T>::from_f(Num<T>::to_f(b.e[e]) * n);
     }
     reinterpret_cast<int4*>(yr)[i] = o.raw;
+  };
+  if constexpr (CACHED) {
+#pragma unroll
+    for (int k = 0; k < kNormCache; ++k) {
+      const int i = threadIdx.x + k * kNormThreads;
+      if (i < nvec) norm_store(i, xc[k]);
+    }
+  } else {
+    for (int i = threadIdx.x; i < nvec; i += kNormThreads) {
+      Vec16<T> a;
+      a.raw = __ldg(reinterpret_cast<const int4*>(xr) + i);
+      norm_store(i, a);
+    }
   }
 }
 
@@ -124,21 +159,26 @@ extern "C" int tread_rmsnorm(const void* x, int64_t ld_x, const void* weight, vo
   TREAD_CHECK_ARG(al16(x) && al16(weight) && al16(y), "rmsnorm: pointers not 16-byte aligned");
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
   const unsigned grid = (unsigned)rows;
+  const bool cached = (long long)hidden * (long long)es / 16 <= (long long)kNormThreads * kNormCache;
+  auto launch = [&](auto tag) {
+    using T = decltype(tag);
+    const T* xp = static_cast<const T*>(x);
+    const T* wp = static_cast<const T*>(weight);
+    T* yp = static_cast<T*>(y);
+    if (cached)
+      rmsnorm_kernel<T, true><<<grid, kNormThreads, 0, st>>>(xp, ld_x, wp, yp, ld_y, hidden, eps);
+    else
+      rmsnorm_kernel<T, false><<<grid, kNormThreads, 0, st>>>(xp, ld_x, wp, yp, ld_y, hidden, eps);
+  };
   switch (dtype) {
     case TREAD_BF16:
-      rmsnorm_kernel<__nv_bfloat16><<<grid, kNormThreads, 0, st>>>(
-          static_cast<const __nv_bfloat16*>(x), ld_x, static_cast<const __nv_bfloat16*>(weight),
-          static_cast<__nv_bfloat16*>(y), ld_y, hidden, eps);
+      launch(__nv_bfloat16());
       break;
     case TREAD_F16:
-      rmsnorm_kernel<__half><<<grid, kNormThreads, 0, st>>>(static_cast<const __half*>(x), ld_x,
-                                                            static_cast<const __half*>(weight),
-                                                            static_cast<__half*>(y), ld_y, hidden, eps);
+      launch(__half());
       break;
     default:
-      rmsnorm_kernel<float><<<grid, kNormThreads, 0, st>>>(static_cast<const float*>(x), ld_x,
-                                                           static_cast<const float*>(weight), static_cast<float*>(y),
-                                                           ld_y, hidden, eps);
+      launch(float());
       break;
   }
   TREAD_CHECK_LAUNCH("rmsnorm_kernel");
