@@ -115,3 +115,16 @@ def test_gather_head_norms_gloo(world):
     assert all(ok for _, ok, _ in res), res
     sels = [s for _, _, s in res]
     assert all(s == sels[0] for s in sels)  # every rank selects the same tokens
+
+
+def test_engine_rejects_graphs_with_tensor_parallel_rows(monkeypatch):
+    """A request graph would capture the all-reduces of a KV-head split: Engine refuses it."""
+    from tread_b200.engine import Engine
+    from tread_b200.store import BlockStore
+
+    model = random_model("tiny", torch.float32)
+    net = tp.TPQwen2Rows.from_model(model)
+    net.world = 2  # as on a rank of a 2-way split
+    with pytest.raises(ValueError):
+        Engine(net, BlockStore(1 << 20), graphs=True)
+    Engine(net, BlockStore(1 << 20), graphs=False)

@@ -74,11 +74,14 @@ class Engine:
     def __init__(self, model, store: BlockStore, graphs=False):
         self.model = model
         self.store = store
+        self.net = rows_of(model)
+        if graphs and getattr(self.net, "world", 1) > 1:
+            # a request graph would capture the tensor-parallel all-reduces: not supported
+            raise ValueError("graphs=True is not supported with tensor-parallel rows")
         self.runner = SubsetRunner(model) if graphs else None
         cfg = model.config
         self.sig = (cfg._name_or_path, str(model.dtype), getattr(cfg, "rope_theta", None),
                     getattr(cfg, "rope_scaling", None))
-        self.net = rows_of(model)
 
     def _sync(self):
         if torch.cuda.is_available():
