@@ -164,13 +164,22 @@ def blend(model, ctx_ids, K, V, candidates, ratio, policy, gen=None, inplace=Fal
 
 def to_cache(K, V):
     """HF DynamicCache over per-layer views (tread/blend.py:182-186). The layers hold the given
-    tensors themselves (no copy of the assembled cache); decoding appends to them as usual."""
+    tensors themselves (no copy of the assembled cache); decoding appends to them as usual.
+    With per-layer cache objects (transformers >= 4.56) the layers are built directly, which
+    skips update()'s lazy initialisation and concatenation with an empty tensor per layer."""
     c = DynamicCache()
-    for l, (k, v) in enumerate(zip(K, V)):
-        c.update(k[..., :0, :], v[..., :0, :], l)  # creates layer l
-        layer = c.layers[l] if hasattr(c, "layers") else None
-        if layer is not None and hasattr(layer, "keys"):
+    try:
+        from transformers.cache_utils import DynamicLayer
+    except ImportError:
+        DynamicLayer = None
+    if DynamicLayer is not None and isinstance(getattr(c, "layers", None), list):
+        for k, v in zip(K, V):
+            layer = DynamicLayer()
+            layer.dtype, layer.device = k.dtype, k.device
             layer.keys, layer.values = k, v
-        else:  # caches without per-layer objects: fall back to the copying update
-            c.update(k, v, l)
+            layer.is_initialized = True
+            c.layers.append(layer)
+        return c
+    for l, (k, v) in enumerate(zip(K, V)):  # caches without per-layer objects: the copying update
+        c.update(k, v, l)
     return c

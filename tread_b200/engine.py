@@ -208,8 +208,9 @@ class Engine:
         offset = P
         for d, b in zip(docs, blocks):
             segs.append((b, offset - b.base, offset))
-            cands.append(torch.arange(offset, offset + len(d), device=d.device))
             offset += len(d)
+        if docs:  # every doc's candidate positions as views of one arange (one launch)
+            cands = list(torch.arange(P, offset, device=docs[0].device).split([len(d) for d in docs]))
         ready = [s for s in segs if s[0].ready is None or s[0].ready.query()]
         pending = [s for s in segs if not (s[0].ready is None or s[0].ready.query())]
         for group in (ready, pending):

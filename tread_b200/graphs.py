@@ -132,10 +132,7 @@ class RequestGraph:
         self.ctx = torch.zeros(T, dtype=torch.int64, device=net.device)
         self.q = torch.zeros(nq, dtype=torch.int64, device=net.device)
         # Every tensor the captured kernels read must outlive the graph: keep them on self.
-        self.cands, off = [], P
-        for n in doc_lens:
-            self.cands.append(torch.arange(off, off + n, device=net.device))
-            off += n
+        self.cands = (list(torch.arange(P, T, device=net.device).split(list(doc_lens))) if doc_lens else [])
 
         def body():
             return compute(self.K, self.V, self.ctx, self.q, self.cands, T, nq, ratio, policy)
