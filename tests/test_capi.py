@@ -98,3 +98,108 @@ def test_deviation_topk_rejects_bad_arguments(over, needle):
 
 def test_deviation_topk_empty_is_noop():
     assert _dev_call(n=0, budget=0) == 0
+
+
+# ---- tensor-parallel selector, rows, attention, elementwise: host-side argument checks -----------
+
+def _norms_call(**over):
+    a = dict(k1=256, v1=256, fst=128, fsh=1024, K1=256, V1=256, cst=128, csh=4096, T=32, pos=256, n=8, H=2,
+             D=128, dtype=C.TREAD_BF16, out=256, ws=256)
+    a.update(over)
+    return C.lib().tread_deviation_head_norms(a["k1"], a["v1"], a["fst"], a["fsh"], a["K1"], a["V1"], a["cst"],
+                                              a["csh"], a["T"], a["pos"], a["n"], a["H"], a["D"], a["dtype"],
+                                              a["out"], a["ws"], None)
+
+
+@pytest.mark.parametrize("over,needle", [
+    (dict(H=0), "Hkv"), (dict(H=33), "Hkv"), (dict(D=96), "D in"), (dict(dtype=9), "dtype"),
+    (dict(k1=258), "aligned"), (dict(fsh=1025), "multiples"), (dict(T=0), "T_cache"), (dict(out=None), "null"),
+])
+def test_deviation_head_norms_rejects_bad_arguments(over, needle):
+    assert _norms_call(**over) == 1
+    assert needle in C.lib().tread_last_error().decode()
+
+
+def _select_call(**over):
+    a = dict(norms=256, n=8, H=2, budget=2, pos=256, dev=256, sel=256, spos=256, ws=256)
+    a.update(over)
+    return C.lib().tread_select_head_norms(a["norms"], a["n"], a["H"], a["budget"], a["pos"], a["dev"], a["sel"],
+                                           a["spos"], a["ws"], None)
+
+
+@pytest.mark.parametrize("over,needle", [
+    (dict(budget=9), "budget"), (dict(budget=-1), "budget"), (dict(H=0), "Hkv"), (dict(sel=None), "sel_idx"),
+    (dict(ws=260), "workspace"), (dict(norms=None), "null"),
+])
+def test_select_head_norms_rejects_bad_arguments(over, needle):
+    assert _select_call(**over) == 1
+    assert needle in C.lib().tread_last_error().decode()
+
+
+def test_tp_selector_empty_is_noop():
+    assert _norms_call(n=0) == 0
+    assert _select_call(n=0, budget=0) == 0
+
+
+def _rope_rows_call(**over):
+    a = dict(qkv=256, ld=(4 + 2 * 2) * 128, pos=256, R=3, Hq=4, Hkv=2, D=128, q=256, K=256, V=256, csh=128 * 16,
+             T=16, by_row=0, inv=[0.5] * 64, scale=1.0, dtype=C.TREAD_BF16)
+    a.update(over)
+    return C.lib().tread_rope_rows(a["qkv"], a["ld"], a["pos"], a["R"], a["Hq"], a["Hkv"], a["D"], a["q"], a["K"],
+                                   a["V"], a["csh"], a["T"], a["by_row"], C.f32_array(a["inv"]), a["scale"],
+                                   a["dtype"], None, None)
+
+
+@pytest.mark.parametrize("over,needle", [
+    (dict(R=-1), "R < 0"), (dict(Hq=3), "heads"), (dict(D=3), "head_dim"), (dict(ld=100), "ld_qkv"),
+    (dict(csh=10), "cache geometry"), (dict(by_row=1, T=2), "kv_by_row"), (dict(dtype=9), "dtype"),
+    (dict(K=None), "null"),
+])
+def test_rope_rows_rejects_bad_arguments(over, needle):
+    assert _rope_rows_call(**over) == 1
+    assert needle in C.lib().tread_last_error().decode()
+
+
+def _attn_call(**over):
+    a = dict(q=256, K=256, V=256, csh=128 * 16, T=16, pos=256, R=3, Hq=4, Hkv=2, D=128, scale=0.1, out=256,
+             dtype=C.TREAD_BF16, flags=0)
+    a.update(over)
+    return C.lib().tread_attn_rows(a["q"], a["K"], a["V"], a["csh"], a["T"], a["pos"], a["R"], a["Hq"], a["Hkv"],
+                                   a["D"], a["scale"], a["out"], a["dtype"], a["flags"], None, None)
+
+
+@pytest.mark.parametrize("over,needle", [
+    (dict(R=-1), "R < 0"), (dict(Hq=3), "heads"), (dict(Hq=34, Hkv=2), "heads"), (dict(D=96), "head_dim"),
+    (dict(csh=10), "cache geometry"), (dict(dtype=9), "dtype"), (dict(flags=2), "flags"), (dict(out=None), "null"),
+])
+def test_attn_rows_rejects_bad_arguments(over, needle):
+    assert _attn_call(**over) == 1
+    assert needle in C.lib().tread_last_error().decode()
+
+
+def test_rows_and_attention_empty_are_noops():
+    assert _rope_rows_call(R=0) == 0
+    assert _attn_call(R=0) == 0
+
+
+@pytest.mark.parametrize("over,needle", [
+    (dict(hidden=4), "16 bytes"), (dict(x=264), "aligned"), (dict(dtype=9), "dtype"), (dict(rows=-1), "rows"),
+])
+def test_rmsnorm_rejects_bad_arguments(over, needle):
+    a = dict(x=256, ldx=64, w=256, y=256, ldy=64, rows=2, hidden=64, eps=1e-6, dtype=C.TREAD_BF16)
+    a.update(over)
+    rc = C.lib().tread_rmsnorm(a["x"], a["ldx"], a["w"], a["y"], a["ldy"], a["rows"], a["hidden"], a["eps"],
+                               a["dtype"], None)
+    assert rc == 1
+    assert needle in C.lib().tread_last_error().decode()
+
+
+@pytest.mark.parametrize("over,needle", [
+    (dict(inter=4), "16 bytes"), (dict(ld=64), "16 bytes"), (dict(y=264), "aligned"), (dict(dtype=9), "dtype"),
+])
+def test_silu_mul_rejects_bad_arguments(over, needle):
+    a = dict(gu=256, ld=128, y=256, ldy=64, rows=2, inter=64, dtype=C.TREAD_BF16)
+    a.update(over)
+    rc = C.lib().tread_silu_mul(a["gu"], a["ld"], a["y"], a["ldy"], a["rows"], a["inter"], a["dtype"], None)
+    assert rc == 1
+    assert needle in C.lib().tread_last_error().decode()
