@@ -301,8 +301,8 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
   uint64_t* v_full = bars + 3;   // [2] V stage loaded
   uint64_t* s_full = bars + 5;   // [2] S buffer written by QK
   // bars 7-8: unused
-  uint64_t* p_full = bars + 9;   // [2] P buffer written by the softmax
-  uint64_t* pv_done = bars + 11; // [2] PV of P buffer b complete (buffer reusable, O stable)
+  uint64_t* p_full = bars + 9;   // [2] P of S buffer b written by the softmax
+  uint64_t* pv_done = bars + 11; // [2] PV of S buffer b's P complete (buffer reusable, O stable)
   uint64_t* k_free = bars + 13;  // [2] K stage read by its QK
   uint64_t* v_free = bars + 15;  // [2] V stage read by its PV
   constexpr int kNumBars = 17;
@@ -402,7 +402,6 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
       constexpr uint32_t idesc_qk = idesc_f16(fmt, 0, kRows, kKeys);
       constexpr uint32_t idesc_pv = idesc_f16(fmt, 1, kRows, kD);
       const uint32_t aQ = smem_u32(sQ), aK = smem_u32(sK), aV = smem_u32(sV);
-      // PV(j): O += P_j V_j, P_j from TMEM (P buffer j%2: 64 columns of packed 16-bit pairs)
       // PV(j): O_h += P_j[:, keys of half h] V_j[keys of half h, :] for h = 0, 1; P of half h sits
       // in S buffer j%2 at columns 64*h .. 64*h+31 (packed pairs)
       auto issue_pv = [&](int j) {
