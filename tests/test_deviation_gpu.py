@@ -40,8 +40,10 @@ def test_golden_selection_matches_reference(cuda):
 
 
 @pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32])
+# more than 8192 candidates take the selector's second path (keys re-read from L2, 8-bit radix)
 @pytest.mark.parametrize("H,D,n,T", [(4, 128, 8192, 8192), (2, 64, 1000, 1032), (4, 128, 777, 4000),
-                                     (8, 128, 100, 300), (1, 256, 33, 40)])
+                                     (8, 128, 100, 300), (1, 256, 33, 40), (2, 128, 20000, 21000),
+                                     (4, 64, 9000, 9100)])
 def test_random_matches_oracle_bit_exact(cuda, dtype, H, D, n, T):
     gen = torch.Generator(device=cuda).manual_seed(H * 1000 + n)
     K1 = torch.randn(H, T, D, device=cuda, generator=gen).to(dtype)
