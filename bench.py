@@ -359,8 +359,10 @@ def run_gpu(args):
     return 0
 
 
-# dram__bytes_read.sum + dram__bytes_write.sum of one launch of this kernel on this workload from an
-# ncu --set full capture (profiles/rope_gather_append_cfg2.md): 469.76 MB read + 421.91 MB written.
+# dram__bytes_read.sum + dram__bytes_write.sum of one launch of this kernel on this workload, a
+# constant cited from one ncu --set full capture of this bench's workload (469.76 MB read +
+# 421.91 MB written; the rest of the writes were still dirty in L2 when the launch ended). The
+# roofline object labels it as cited, not measured by this run.
 TRAFFIC_PER_LAUNCH = 469762048 + 421905920
 
 

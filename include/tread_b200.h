@@ -143,6 +143,12 @@ int tread_select_head_norms(const float* norms, int n, int Hkv, int budget, cons
  *     that device current), so make that first call before any stream capture;
  *   - every call clears the ticket words on `stream` and then reuses the shared array, so calls
  *     that overlap on the GPU (different streams, or different host threads) race: order them;
+ *   - err_flag (optional, device unsigned[1], may be NULL) receives this call's out-of-range
+ *     flag in stream order: 1 if a candidate position lay outside [0, T_cache) (that candidate's
+ *     deviation is NaN and it ranks first), else 0. It is copied out of the shared array, so it
+ *     needs no scratch from the caller;
+ *   - the array's device address is cached per device for the primary context, so it does not
+ *     survive cudaDeviceReset;
  *   - it calls no cudaMalloc / cudaFree.
  */
 #define TREAD_NOALLOC_MAX_CANDIDATES 65536
@@ -150,7 +156,8 @@ int tread_deviation_topk_noalloc(const void* k1, const void* v1, int64_t fresh_s
                                  int64_t fresh_stride_head, const void* K1, const void* V1,
                                  int64_t cache_stride_tok, int64_t cache_stride_head, int64_t T_cache,
                                  const int64_t* cand_pos, int n, int Hkv, int D, int budget, int dtype,
-                                 int64_t* sel_idx, int64_t* sel_pos, tread_stream_t stream);
+                                 int64_t* sel_idx, int64_t* sel_pos, unsigned* err_flag,
+                                 tread_stream_t stream);
 
 /*
  * RoPE at each row's absolute position + splice of the row's K/V into the layer cache.

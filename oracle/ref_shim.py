@@ -18,11 +18,18 @@ without touching the reference sources:
 import os
 import sys
 
-REFERENCE_ROOT = os.environ.get("TREAD_REFERENCE_ROOT", "/root/reference")
+# The reference checkout's root (the directory that holds the `tread` package): taken from the
+# TREAD_REFERENCE_ROOT environment variable, or set with `set_root()` before `install()`.
+REFERENCE_ROOT = os.environ.get("TREAD_REFERENCE_ROOT", "")
+
+
+def set_root(path):
+    global REFERENCE_ROOT
+    REFERENCE_ROOT = path
 
 
 def available() -> bool:
-    return os.path.isdir(os.path.join(REFERENCE_ROOT, "tread"))
+    return bool(REFERENCE_ROOT) and os.path.isdir(os.path.join(REFERENCE_ROOT, "tread"))
 
 
 _patched = False
@@ -32,7 +39,7 @@ def install():
     """Patch transformers once and put the reference on sys.path. Returns the `tread` package."""
     global _patched
     if not available():
-        raise RuntimeError(f"tread reference not found under {REFERENCE_ROOT}")
+        raise RuntimeError(f"tread reference not found under {REFERENCE_ROOT!r}: set TREAD_REFERENCE_ROOT")
     if not _patched:
         from transformers import DynamicCache
         from transformers.models.qwen2 import modeling_qwen2 as mq

@@ -1,9 +1,9 @@
 """Generate the golden fixtures in tests/golden/ by running the UNMODIFIED tread reference.
 
-Run in a container that holds the reference sources (default /root/reference, override with
-TREAD_REFERENCE_ROOT):
+Run where the reference sources are checked out, naming their root (the directory that holds
+the `tread` package) with --reference or the TREAD_REFERENCE_ROOT environment variable:
 
-    python tests/golden/make_golden.py
+    python tests/golden/make_golden.py --reference <root> [fixture ...]
 
 The reference is imported through oracle/ref_shim.py (transformers 5.x attribute renames
 only). Models are seeded random-init Qwen2 architectures (tread_b200/configs.py): the HF
@@ -22,6 +22,16 @@ Fixtures:
                 Engine.prefill (tread/engine.py:98-136) cold then reordered requests, ratios 0 /
                 0.2 deviation / 1.0 boundary: stats, selected positions, first-token logits, and
                 prefill_full logits (the KL reference).
+  engine_bf16_tiny.npz, engine_bf16_7b3l.npz
+                the same requests on bf16 models (the tiny architecture, and the configs[2]
+                Qwen2.5-7B architecture cut to 3 layers with the full 256 + 16 x 496 + 64 request),
+                ratios 0 / 0.2 / 0.5 deviation / 1.0 boundary, with the reference's own bf16
+                deviation values; the tiny fixture also holds the reference's layer-1 k1, v1 and
+                gathered K1, V1 of the 0.2 request (bf16 bits) for the selection-convention gate.
+  store_engine_bf16.npz
+                a sequence of requests on the bf16 tiny model through a store whose GPU tier holds
+                about two doc blocks and whose pinned tier holds three: all eight StoreStats
+                counters, both tiers' key order and the first-token logits after every request.
 """
 import os
 import sys
@@ -191,7 +201,19 @@ def make_store(tread):
         gpu_keys=np.array(gpu_keys), cpu_keys=np.array(cpu_keys))
 
 
-def run_engine(model, prefix, docs, query, reorder):
+RATIOS = (("r0", 0.0, "deviation"), ("r02", 0.2, "deviation"), ("b10", 1.0, "boundary"))
+RATIOS_BF16 = (("r0", 0.0, "deviation"), ("r02", 0.2, "deviation"), ("r05", 0.5, "deviation"),
+               ("b10", 1.0, "boundary"))
+
+
+def logits_out(logits):
+    """fp32 logits as they are; a bf16 model's logits as their exact bf16 bits."""
+    if logits.dtype == torch.bfloat16:
+        return bf16_bits(logits)
+    return logits.float().numpy()
+
+
+def run_engine(model, prefix, docs, query, reorder, ratios=RATIOS, layer1_tag=None):
     import tread.blend as tb
     import tread.engine as te
     from tread.engine import Engine, prefill_full
@@ -199,13 +221,28 @@ def run_engine(model, prefix, docs, query, reorder):
 
     cap = {}
     orig_blend = te.blend
+    orig_dev = tb.layer1_deviation
 
     def blend_spy(*a, **kw):
         K, V, S, eff = orig_blend(*a, **kw)
         cap["S"] = S.clone()
         return K, V, S, eff
 
+    def dev_spy(model_, ctx_ids, K, V, all_c, inplace=False):
+        K1 = K[1][:, :, all_c].clone()
+        V1 = V[1][:, :, all_c].clone()
+        dev, h, K0, V0 = orig_dev(model_, ctx_ids, K, V, all_c, inplace=inplace)
+        cap["dev"] = dev.clone()
+        if cap.get("want_layer1"):
+            # k1/v1 exactly as layer1_deviation forms them (tread/blend.py:127-128)
+            layers = model_.model.layers
+            _, k1, v1 = tb._qkv(layers[1], model_, layers[1].input_layernorm(h), all_c,
+                                tb._subset_ctx(model_, all_c, K[0].shape[2], h)[0])
+            cap.update(k1=k1[0].clone(), v1=v1[0].clone(), K1=K1[0], V1=V1[0], all_c=all_c.clone())
+        return dev, h, K0, V0
+
     te.blend = blend_spy
+    tb.layer1_deviation = dev_spy
     out = {}
     try:
         with torch.inference_mode():
@@ -213,23 +250,31 @@ def run_engine(model, prefix, docs, query, reorder):
             _, _, st1 = eng.prefill(prefix, docs, query)
             order = [docs[i] for i in reorder]
             out["stats_cold"] = np.array([st1.hits, st1.misses, st1.tokens_reused, st1.tokens_prefilled], np.int64)
-            for tag, ratio, policy in (("r0", 0.0, "deviation"), ("r02", 0.2, "deviation"),
-                                       ("b10", 1.0, "boundary")):
+            for tag, ratio, policy in ratios:
                 cap.pop("S", None)
+                cap.pop("dev", None)
+                cap["want_layer1"] = tag == layer1_tag
                 logits, _, st = eng.prefill(prefix, order, query, ratio=ratio, policy=policy)
-                out[f"logits_{tag}"] = logits.float().numpy()
+                out[f"logits_{tag}"] = logits_out(logits)
+                if "dev" in cap:
+                    out[f"dev_{tag}"] = cap["dev"].float().numpy()
+                if tag == layer1_tag:
+                    for k in ("k1", "v1", "K1", "V1"):
+                        out[f"l1_{k}"] = bf16_bits(cap[k])
+                    out["l1_all_c"] = cap["all_c"].numpy()
                 out[f"stats_{tag}"] = np.array([st.hits, st.misses, st.tokens_reused, st.tokens_prefilled],
                                                np.int64)
                 out[f"eff_{tag}"] = np.float64(st.recompute_eff)
                 if "S" in cap:
                     out[f"S_{tag}"] = cap["S"].numpy()
             ref, _, _ = prefill_full(model, prefix, order, query)
-            out["logits_full"] = ref.float().numpy()
+            out["logits_full"] = logits_out(ref)
             s = eng.store.stats
             out["store_stats"] = np.array([s.hits, s.misses, s.evictions, s.bytes_used, s.cpu_hits, s.offloads,
                                            s.cpu_evictions, s.cpu_bytes_used], np.int64)
     finally:
         te.blend = orig_blend
+        tb.layer1_deviation = orig_dev
     out.update(prefix=prefix.numpy(), query=query.numpy(), reorder=np.array(reorder, np.int64))
     for i, d in enumerate(docs):
         out[f"doc{i}"] = d.numpy()
@@ -256,11 +301,92 @@ def make_engine_cfg1(tread):
     np.savez_compressed(os.path.join(HERE, "engine_cfg1.npz"), **out)
 
 
+def make_engine_bf16_tiny(tread):
+    """The tiny architecture in bf16: the engine_tiny request at ratios 0 / 0.2 / 0.5 / 1.0, the
+    reference's bf16 deviation values, and its layer-1 tensors of the 0.2 request."""
+    model = random_model("tiny", dtype=torch.bfloat16)
+    prefix, docs, query = tiny_request(model.config.vocab_size)
+    out = run_engine(model, prefix, docs, query, [2, 0, 1], ratios=RATIOS_BF16, layer1_tag="r02")
+    np.savez_compressed(os.path.join(HERE, "engine_bf16_tiny.npz"), **out)
+
+
+def make_engine_bf16_7b3l(tread):
+    """BASELINE configs[2] in bf16: the Qwen2.5-7B architecture (hidden 3584, 28/4 heads, head_dim
+    128, MLP 18944, vocab 152064) cut to 3 layers so the reference runs on host cores; the full
+    request shape, 256 prefix + 16 docs x 496 + 64 query, cold then one reordering."""
+    model = random_model("qwen2.5-7b", dtype=torch.bfloat16, layers=3)
+    g = torch.Generator().manual_seed(2)
+    V = model.config.vocab_size
+    prefix = random_tokens(256, V, g)
+    docs = [random_tokens(496, V, g) for _ in range(16)]
+    query = random_tokens(64, V, g)
+    reorder = torch.randperm(16, generator=g).tolist()
+    out = run_engine(model, prefix, docs, query, reorder, ratios=RATIOS_BF16)
+    np.savez_compressed(os.path.join(HERE, "engine_bf16_7b3l.npz"), **out)
+
+
+# Requests of the store-pressure sequence: (doc indices in request order, ratio); policy deviation.
+STORE_SEQ = (([0, 1, 2], 0.0), ([2, 0, 1], 0.2), ([3, 4], 0.0), ([0, 5, 3], 0.2), ([1, 2, 4, 5], 0.0),
+             ([5, 4, 3, 2, 1, 0], 0.2), ([0, 1], 0.0), ([4, 0], 0.5))
+STORE_DOC_LENS = (40, 33, 47, 29, 52, 36)
+
+
+def make_store_engine_bf16(tread):
+    """Engine requests through a small two-tier store (tread/store.py:56-125 decisions under
+    eviction, offload and CPU-tier hits), bf16 tiny model. Block bytes = 2 * L * Hkv * n * D * 2."""
+    from tread.engine import Engine
+    from tread.store import BlockStore
+
+    torch.Tensor.pin_memory = lambda self, *a, **k: self  # no CUDA driver here; changes no decision
+    model = random_model("tiny", dtype=torch.bfloat16)
+    cfg = model.config
+    per_tok = 2 * cfg.num_hidden_layers * cfg.num_key_value_heads * (cfg.hidden_size // cfg.num_attention_heads) * 2
+    gpu_budget, cpu_budget = per_tok * 100, per_tok * 130
+    g = torch.Generator().manual_seed(11)
+    prefix = random_tokens(16, cfg.vocab_size, g)
+    docs = [random_tokens(n, cfg.vocab_size, g) for n in STORE_DOC_LENS]
+    query = random_tokens(8, cfg.vocab_size, g)
+    eng = Engine(model, BlockStore(gpu_budget, cpu_budget_bytes=cpu_budget))
+    req_stats, store_stats, gpu_keys, cpu_keys, logits, effs = [], [], [], [], [], []
+    with torch.inference_mode():
+        for idx, ratio in STORE_SEQ:
+            lg, _, st = eng.prefill(prefix, [docs[i] for i in idx], query, ratio=ratio)
+            req_stats.append([st.hits, st.misses, st.tokens_reused, st.tokens_prefilled])
+            effs.append(st.recompute_eff)
+            s = eng.store.stats
+            store_stats.append([s.hits, s.misses, s.evictions, s.bytes_used, s.cpu_hits, s.offloads,
+                                s.cpu_evictions, s.cpu_bytes_used])
+            gpu_keys.append(",".join(eng.store.blocks.keys()))
+            cpu_keys.append(",".join(eng.store.cpu_blocks.keys()))
+            logits.append(bf16_bits(lg))
+    out = dict(seq_docs=np.concatenate([np.array(i, np.int64) for i, _ in STORE_SEQ]),
+               seq_lens=np.array([len(i) for i, _ in STORE_SEQ], np.int64),
+               seq_ratio=np.array([r for _, r in STORE_SEQ], np.float64),
+               prefix=prefix.numpy(), query=query.numpy(), gpu_budget=np.int64(gpu_budget),
+               cpu_budget=np.int64(cpu_budget), req_stats=np.array(req_stats, np.int64),
+               store_stats=np.array(store_stats, np.int64), eff=np.array(effs, np.float64),
+               gpu_keys=np.array(gpu_keys), cpu_keys=np.array(cpu_keys), logits=np.stack(logits))
+    for i, d in enumerate(docs):
+        out[f"doc{i}"] = d.numpy()
+    np.savez_compressed(os.path.join(HERE, "store_engine_bf16.npz"), **out)
+
+
+ALL = ["rope", "deviation", "attention", "store", "engine_tiny", "engine_cfg1", "engine_bf16_tiny",
+       "engine_bf16_7b3l", "store_engine_bf16"]
+
+
 def main():
+    import argparse
+
+    ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
+    ap.add_argument("--reference", help="root of the reference checkout (else TREAD_REFERENCE_ROOT)")
+    ap.add_argument("fixtures", nargs="*", default=[], help="fixtures to generate (default: all): " + ", ".join(ALL))
+    a = ap.parse_args()
+    if a.reference:
+        ref_shim.set_root(a.reference)
     tread = ref_shim.install()
     torch.set_num_threads(min(8, os.cpu_count() or 1))
-    which = sys.argv[1:] or ["rope", "deviation", "attention", "store", "engine_tiny", "engine_cfg1"]
-    for w in which:
+    for w in a.fixtures or ALL:
         print("generating", w, flush=True)
         globals()[f"make_{w}"](tread)
 

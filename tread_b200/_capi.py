@@ -39,7 +39,7 @@ SIGNATURES = {
     "tread_deviation_topk_noalloc": (
         ctypes.c_int,
         [P, P, I64, I64, P, P, I64, I64, I64, P, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int,
-         ctypes.c_int, P, P, P],
+         ctypes.c_int, P, P, P, P],
     ),
     "tread_deviation_head_norms": (
         ctypes.c_int,

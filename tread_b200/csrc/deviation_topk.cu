@@ -676,7 +676,8 @@ constexpr int kMaxDevices = 128;
 std::mutex g_scratch_mu;
 void* g_scratch_addr[kMaxDevices] = {};  // device address of g_selector_scratch, per device
 
-// Device address of the static scratch on the current device, looked up once per device.
+// Device address of the static scratch on the current device, looked up once per device. The
+// cached address belongs to the device's primary context: it does not survive cudaDeviceReset.
 int scratch_address(void** out) {
   int dev = -1;
   TREAD_CHECK_CUDA(cudaGetDevice(&dev));
@@ -703,7 +704,8 @@ extern "C" int tread_deviation_topk_noalloc(const void* k1, const void* v1, int6
                                             int64_t fresh_stride_head, const void* K1, const void* V1,
                                             int64_t cache_stride_tok, int64_t cache_stride_head, int64_t T_cache,
                                             const int64_t* cand_pos, int n, int Hkv, int D, int budget, int dtype,
-                                            int64_t* sel_idx, int64_t* sel_pos, tread_stream_t stream) {
+                                            int64_t* sel_idx, int64_t* sel_pos, unsigned* err_flag,
+                                            tread_stream_t stream) {
   using namespace tread;
   TREAD_CHECK_ARG(n >= 0 && n <= kNoAllocMaxCandidates,
                   "deviation_topk_noalloc: n=%d candidates exceeds the static scratch maximum of %d", n,
@@ -715,7 +717,14 @@ extern "C" int tread_deviation_topk_noalloc(const void* k1, const void* v1, int6
   // The array keeps the previous call's contents: the ticket and error words must start at zero.
   TREAD_CHECK_CUDA(cudaMemsetAsync(scratch, 0, kNoAllocTicketBytes, reinterpret_cast<cudaStream_t>(stream)));
   float* dev = reinterpret_cast<float*>(static_cast<unsigned char*>(scratch) + kNoAllocTicketBytes);
-  return tread_deviation_topk(k1, v1, fresh_stride_tok, fresh_stride_head, K1, V1, cache_stride_tok,
-                              cache_stride_head, T_cache, cand_pos, n, Hkv, D, budget, dtype, dev, sel_idx, sel_pos,
-                              scratch, stream);
+  const int st = tread_deviation_topk(k1, v1, fresh_stride_tok, fresh_stride_head, K1, V1, cache_stride_tok,
+                                      cache_stride_head, T_cache, cand_pos, n, Hkv, D, budget, dtype, dev, sel_idx,
+                                      sel_pos, scratch, stream);
+  if (st != TREAD_OK || err_flag == nullptr) return st;
+  // Word 1 of the scratch is this call's out-of-range flag (cleared above): hand it to the caller
+  // in stream order, before a later call clears it again.
+  TREAD_CHECK_CUDA(cudaMemcpyAsync(err_flag, static_cast<unsigned char*>(scratch) + sizeof(unsigned),
+                                   sizeof(unsigned), cudaMemcpyDeviceToDevice,
+                                   reinterpret_cast<cudaStream_t>(stream)));
+  return TREAD_OK;
 }

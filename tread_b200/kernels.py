@@ -149,6 +149,12 @@ def workspace(device, stream=None):
     return ws
 
 
+def selector_flags(device):
+    """Word 1 of the default-stream selector workspace of `device` (a one-element int32 view): the
+    sticky flag the selector kernels set when a candidate position lies outside the cache."""
+    return workspace(device)[1:2]
+
+
 def _rows_view(t, name):
     """(tensor, token stride, head stride) of a [H, n, D] or [1, H, n, D] view with unit last stride."""
     C.require_cuda(t, name)

@@ -135,8 +135,11 @@ class Qwen2Rows:
                 torch.zeros(shape, dtype=self.dtype, device=self.device))
 
     def check_errors(self):
-        """Raise if a kernel flagged an out-of-range row position (costs a device sync)."""
-        e = int(self.err.max().item())
+        """Raise if a kernel flagged an out-of-range row position: the row kernels' error word and
+        the selector's sticky flag, read with one device sync."""
+        sel = kernels.selector_flags(self.device)
+        e = int(torch.cat([self.err, sel]).max().item())
         if e:
             self.err.zero_()
+            sel.zero_()
             raise RuntimeError(f"tread_b200 kernel reported an out-of-range position (flags {e:#x})")

@@ -191,9 +191,13 @@ class TPQwen2Rows(Qwen2Rows):
         return kernels.select_head_norms(gather_head_norms(norms, self.group), cand_pos, budget)
 
     def check_errors(self):
-        e = self.err.max()
+        """Raise on every rank if a kernel on any rank flagged an error (row kernels' error word
+        or the selector's out-of-range flag), with one all-reduce."""
+        sel = kernels.selector_flags(self.device)
+        e = torch.cat([self.err, sel]).max()
         if self.world > 1:
             dist.all_reduce(e, op=dist.ReduceOp.MAX, group=self.group)
         if int(e.item()):
             self.err.zero_()
+            sel.zero_()
             raise RuntimeError(f"tread_b200 kernel reported an error on some rank (flags {int(e):#x})")
