@@ -69,6 +69,10 @@ def parse():
     ap.add_argument("--dp-rounds", type=int, default=30, help="timed serving rounds (one request per replica each)")
     ap.add_argument("--no-tp", action="store_true",
                     help="skip the KV-head tensor-parallel TTFT legs (configs[2] 7B, configs[3] 32B)")
+    ap.add_argument("--no-cpu-ttft", action="store_true",
+                    help="skip the TTFT CPU baseline (the request path's CPU restatement on host cores)")
+    ap.add_argument("--cpu-ttft-7b", type=int, default=1,
+                    help="1: also time the configs[2] 7B request at 0.2 on host cores (needs ~20 GB host RAM)")
     return ap.parse_args()
 
 
@@ -218,6 +222,184 @@ def cpu_assembly_rate(nsteps_min, seconds, seed, nblk, host_pool=16):
             "host_pool": host_pool}
 
 
+def host_cpu_info():
+    """CPU model, logical and physical cores of this host, and torch's intra-op thread count."""
+    model, phys = "unknown", set()
+    try:
+        with open("/proc/cpuinfo") as f:
+            cur = {}
+            for line in f:
+                if ":" in line:
+                    k, v = (x.strip() for x in line.split(":", 1))
+                    cur[k] = v
+                    if k == "model name":
+                        model = v
+                elif cur:
+                    phys.add((cur.get("physical id"), cur.get("core id")))
+                    cur = {}
+            if cur:
+                phys.add((cur.get("physical id"), cur.get("core id")))
+    except OSError:
+        pass
+    return {"cpu_model": model, "logical_cpus": os.cpu_count(), "physical_cores": len(phys) or None,
+            "torch_threads": torch.get_num_threads()}
+
+
+def host_ram_gb():
+    try:
+        with open("/proc/meminfo") as f:
+            for line in f:
+                if line.startswith("MemAvailable:"):
+                    return int(line.split()[1]) / 1e6
+    except OSError:
+        pass
+    return 0.0
+
+
+def run_ttft_cpu(args):
+    """TTFT CPU baseline: the request path's CPU restatement (oracle/engine_port.py, pinned against
+    the reference's own outputs) on this host's cores, timed like the reference's bench
+    (bench/bench_scaling.py:64-66: perf_counter, median, the cold pass excluded).
+      Qwen2.5-0.5B architecture, fp32, prefix 32 + docs A-D of 250 + query 16; the cold
+        request A,B,C,D, then warm requests D,B,A,C at ratios 0 and 0.2 (median of 5);
+      the 7B architecture in bf16, 256 + 16 x 496 + 64 tokens, at 0.2 (and 0): blocks
+        seeded with random values under the request's keys (warm requests do the same work whatever
+        the values), 1 untimed request, then the median of 2."""
+    from oracle.engine_port import CpuPort, random_bf16_model
+    from tread_b200.configs import random_model, random_tokens
+
+    torch.set_num_threads(os.cpu_count() or 1)
+    out = {"kind": "port", "impl": "oracle/engine_port.py (CPU restatement of tread/engine.py:98-136)",
+           **host_cpu_info()}
+    model = random_model("qwen2.5-0.5b")
+    g = torch.Generator().manual_seed(0)
+    V = model.config.vocab_size
+    prefix = random_tokens(32, V, g)
+    docs = [random_tokens(250, V, g) for _ in range(4)]
+    query = random_tokens(16, V, g)
+    port = CpuPort(model)
+    port.prefill(prefix, docs, query)  # cold: fills the blocks
+    order = [docs[i] for i in (3, 1, 0, 2)]
+    cfg0 = {}
+    for ratio in (0.0, 0.2):
+        ts = []
+        for _ in range(6):
+            t0 = time.perf_counter()
+            logits, st, _ = port.prefill(prefix, order, query, ratio=ratio)
+            int(logits.argmax())
+            ts.append(time.perf_counter() - t0)
+        cfg0[str(ratio)] = {"p50_ms": round(statistics.median(ts[1:]) * 1e3, 1)}
+    out["configs[0]"] = {"workload": "Qwen2.5-0.5B architecture fp32, 32 + 4x250 + 16, order D,B,A,C warm",
+                         "ratios": cfg0}
+    del port, model
+    if args.cpu_ttft_7b:
+        ram = host_ram_gb()
+        if ram < 40:
+            out["configs[2]"] = {"skipped": f"{ram:.0f} GB of host RAM available, 40 GB wanted"}
+        else:
+            t_init = time.perf_counter()
+            model = random_bf16_model("qwen2.5-7b", seed=args.seed)
+            V = model.config.vocab_size
+            g = torch.Generator().manual_seed(args.seed + 3)
+            prefix = random_tokens(256, V, g)
+            docs = [random_tokens(496, V, g) for _ in range(16)]
+            query = random_tokens(64, V, g)
+            port = CpuPort(model)
+            port.seed_blocks(prefix, docs, torch.Generator().manual_seed(1))
+            init_s = time.perf_counter() - t_init
+            pg = torch.Generator().manual_seed(args.seed + 5)
+            res = {}
+            for ratio in (0.0, 0.2):
+                ts = []
+                for _ in range(3):
+                    order = [docs[i] for i in torch.randperm(16, generator=pg).tolist()]
+                    t0 = time.perf_counter()
+                    logits, st, _ = port.prefill(prefix, order, query, ratio=ratio)
+                    int(logits.argmax())
+                    ts.append(time.perf_counter() - t0)
+                res[str(ratio)] = {"p50_ms": round(statistics.median(ts[1:]) * 1e3, 1),
+                                   "stages_ms": {k: round(v * 1e3, 1) for k, v in st["t"].items()}}
+            out["configs[2]"] = {"workload": "Qwen2.5-7B architecture bf16, 256 + 16x496 + 64, reordered, warm",
+                                 "init_s": round(init_s, 1), "ratios": res}
+            del port, model
+    return out
+
+
+def run_ttft_cfg0_gpu(args, dev):
+    """configs[0] on the GPU engine, for the CPU baseline's first workload: the same model (fp32,
+    Qwen2.5-0.5B architecture, the same seeded weights) and request, cold then warm D,B,A,C at
+    ratios 0 and 0.2, host ids in and the first token out, median of 5 after 2 untimed."""
+    from tread_b200 import BlockStore, Engine
+    from tread_b200.configs import random_model, random_tokens
+
+    model = random_model("qwen2.5-0.5b").to(dev)
+    g = torch.Generator().manual_seed(0)
+    V = model.config.vocab_size
+    prefix = random_tokens(32, V, g)
+    docs = [random_tokens(250, V, g) for _ in range(4)]
+    query = random_tokens(16, V, g)
+    eng = Engine(model, BlockStore(8 << 30))
+    eng.prefill(prefix, docs, query)
+    order = [docs[i] for i in (3, 1, 0, 2)]
+    res = {}
+    for ratio in (0.0, 0.2):
+        ts = []
+        for rep in range(7):
+            torch.cuda.synchronize(dev)
+            t0 = time.perf_counter()
+            logits, cache, st = eng.prefill(prefix, order, query, ratio=ratio)
+            int(logits.argmax().item())
+            ts.append(time.perf_counter() - t0)
+            del cache
+        res[str(ratio)] = {"p50_ms": round(statistics.median(ts[2:]) * 1e3, 2)}
+    del eng, model
+    torch.cuda.empty_cache()
+    return {"workload": "configs[0]: Qwen2.5-0.5B architecture fp32, 32 + 4x250 + 16, order D,B,A,C warm",
+            "ratios": res}
+
+
+def pcie_peak(dev, nbytes=256 << 20, reps=5):
+    """Pinned host <-> HBM copy bandwidth of this box, one direction at a time and both at once
+    (cudaMemcpyAsync on two streams), best of `reps`, CUDA events: the ceiling of the e2e leg."""
+    h_src = torch.empty(nbytes, dtype=torch.uint8).pin_memory()
+    h_dst = torch.empty(nbytes, dtype=torch.uint8).pin_memory()
+    d_a = torch.empty(nbytes, dtype=torch.uint8, device=dev)
+    d_b = torch.empty(nbytes, dtype=torch.uint8, device=dev)
+    s1, s2 = torch.cuda.Stream(dev), torch.cuda.Stream(dev)
+
+    def timed(fn):
+        best = None
+        for _ in range(reps):
+            torch.cuda.synchronize(dev)
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record(s1)
+            s2.wait_stream(s1)
+            fn()
+            s1.wait_stream(s2)
+            b.record(s1)
+            torch.cuda.synchronize(dev)
+            ms = a.elapsed_time(b)
+            best = ms if best is None else min(best, ms)
+        return best
+
+    def h2d():
+        with torch.cuda.stream(s1):
+            d_a.copy_(h_src, non_blocking=True)
+
+    def d2h():
+        with torch.cuda.stream(s2):
+            h_dst.copy_(d_b, non_blocking=True)
+
+    def both():
+        h2d()
+        d2h()
+
+    ms_in, ms_out, ms_both = timed(h2d), timed(d2h), timed(both)
+    return {"h2d_gbs": round(nbytes / (ms_in * 1e-3) / 1e9, 1), "d2h_gbs": round(nbytes / (ms_out * 1e-3) / 1e9, 1),
+            "duplex_gbs": round(2 * nbytes / (ms_both * 1e-3) / 1e9, 1),
+            "how": f"{nbytes >> 20} MiB pinned copies, best of {reps}; duplex = H2D and D2H on two streams at once"}
+
+
 def run_reference(args):
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
@@ -323,6 +505,10 @@ def run_gpu(args):
         ttft_tp["qwen2.5-32b"] = run_ttft_tp(args, dev, world, rank, "qwen2.5-32b", 512, 32, 500, 128)
     serving = None if args.no_dp else run_serving_dp(args, dev, world, rank)
 
+    if ttft is not None:
+        ttft["configs[0]_gpu"] = run_ttft_cfg0_gpu(args, dev)
+        if rank == 0 and not args.no_cpu_ttft:
+            ttft["cpu_baseline"] = run_ttft_cpu(args)
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         r = cpu_assembly_rate(3, args.cpu_seconds, args.seed, args.blocks)
@@ -491,7 +677,7 @@ def run_ttft_tp(args, dev, world, rank, arch, prefix_len, ndocs, doc_len, q_len)
     pg = torch.Generator().manual_seed(args.seed + 13)
     res = {}
     for ratio in (0.0, 0.2):
-        times, stages = [], []
+        times, stages, colls = [], [], []
         for rep in range(2 + args.ttft_reps):
             order = [docs[i] for i in torch.randperm(ndocs, generator=pg).tolist()]
             barrier(world)
@@ -504,9 +690,26 @@ def run_ttft_tp(args, dev, world, rank, arch, prefix_len, ndocs, doc_len, q_len)
             if rep >= 2:
                 times.append(max_over_ranks(t1 - t0, world, dev))
                 stages.append(st.t)
+        if world > 1:
+            # one more request of the same kind with every collective bracketed by CUDA events
+            # (kept out of the timed requests above): device ms per collective kind, max over ranks
+            order = [docs[i] for i in torch.randperm(ndocs, generator=pg).tolist()]
+            net.collective_events = []
+            barrier(world)
+            logits_c, cache, _ = eng.prefill(prefix, order, query, ratio=ratio)
+            int(logits_c.argmax().item())
+            del cache
+            cms = net.collective_ms()
+            net.collective_events = None
+            names = ("o_proj_allreduce", "down_proj_allreduce", "head_norms_allgather")
+            vals = [max_over_ranks(cms.get(k, 0.0), world, dev) for k in names]
+            colls = {k: round(v, 3) for k, v in zip(names, vals)}
         r = {"p50_ms": round(statistics.median(times) * 1e3, 2), "min_ms": round(min(times) * 1e3, 2),
              "stages_p50_ms": {k: round(statistics.median(s_[k] for s_ in stages) * 1e3, 2) for k in stages[0]},
              "recompute_eff": round(st.recompute_eff, 4), "hits": st.hits, "misses": st.misses}
+        if colls:
+            r["collective_device_ms_per_request"] = colls
+            r["collective_share_of_p50"] = round(sum(colls.values()) / r["p50_ms"], 3)
         if ratio == 0.2:
             ref, _, _ = prefill_full(net, prefix, order, query)
             r["kl_vs_full_prefill"] = round(kl_div(logits, ref), 5)
@@ -757,10 +960,15 @@ def run_e2e(args, dev, pool_k, pool_v, ids, deltas, inv, world, rank):
     ms = start.elapsed_time(end) / args.e2e_steps
     ms = max_over_ranks(ms, world, dev)
     blk_bytes = pool_k[0].nbytes + pool_v[0].nbytes
+    moved = nblk * blk_bytes + out_k.nbytes + out_v.nbytes
+    peak = pcie_peak(dev)
+    pcie_gbs = moved / (ms * 1e-3) / 1e9
     return {"value": round(world * algorithmic_bytes(nblk) / (ms * 1e-3) / 1e9, 2), "unit": "GB/s",
             "ms_per_step": round(ms, 3), "h2d_bytes_per_step": nblk * blk_bytes,
             "d2h_bytes_per_step": out_k.nbytes + out_v.nbytes, "kernel_launches_per_step": nblk,
-            "path": "pinned host blocks -> tread_kv_fetch -> tread_rope_gather_append -> tread_kv_spill_rows"}
+            "path": "pinned host blocks -> tread_kv_fetch -> tread_rope_gather_append -> tread_kv_spill_rows",
+            "pcie": {"achieved_gbs": round(pcie_gbs, 1), "peak": peak,
+                     "frac_of_duplex_peak": round(pcie_gbs / peak["duplex_gbs"], 3)}}
 
 
 def run_only_ttft(args):

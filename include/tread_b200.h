@@ -173,7 +173,8 @@ int tread_deviation_topk_noalloc(const void* k1, const void* v1, int64_t fresh_s
  * A position outside [0, T_cache) skips its row and sets bit 0 of *err_flag (may be NULL).
  * kv_by_row = 1 writes row r's k/v to cache row r instead of row pos[r] (dense [Hkv, R, D]
  * outputs, e.g. the fresh layer-1 rows of the deviation selector, blend.py:128); q_out may be
- * NULL to skip the q heads.
+ * NULL to skip the q heads. With q_out NULL, Hq = 0 declares rows of [k heads | v heads] only
+ * (a k/v-only projection: the selector needs no layer-1 queries, blend.py:127-129).
  */
 int tread_rope_rows(const void* qkv, int64_t ld_qkv, const int64_t* pos, int R, int Hq, int Hkv, int D,
                     void* q_out, void* K_cache, void* V_cache, int64_t cache_stride_head,

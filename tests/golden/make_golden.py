@@ -28,6 +28,9 @@ Fixtures:
                 ratios 0 / 0.2 / 0.5 deviation / 1.0 boundary, with the reference's own bf16
                 deviation values; the tiny fixture also holds the reference's layer-1 k1, v1 and
                 gathered K1, V1 of the 0.2 request (bf16 bits) for the selection-convention gate.
+  server.npz    the reference's HTTP app on its own engine (tiny fp32 model, character-level stub
+                tokenizer): each response's text, finish reason, usage and reuse stats, and
+                /metrics after the sequence.
   store_engine_bf16.npz
                 a sequence of requests on the bf16 tiny model through a store whose GPU tier holds
                 about two doc blocks and whose pinned tier holds three: all eight StoreStats
@@ -371,8 +374,62 @@ def make_store_engine_bf16(tread):
     np.savez_compressed(os.path.join(HERE, "store_engine_bf16.npz"), **out)
 
 
+def make_server(tread):
+    """The reference's HTTP app (tread/server.py:131-237) on its own engine, tiny fp32 model, the
+    character-level stub tokenizer, a store small enough to evict and offload: the response of
+    each request in stub_tokenizer.SERVER_REQUESTS (timing fields dropped) and /metrics after
+    the last one. Also records the smallest gap between the two largest logits met by any greedy
+    step, so a test can tell that argmax decisions are not knife-edge."""
+    import json
+
+    import tread.server as ts
+    from fastapi.testclient import TestClient
+    from tread.engine import Engine
+    from tread.store import BlockStore
+
+    sys.path.insert(0, HERE)
+    from stub_tokenizer import SERVER_REQUESTS, StubTokenizer
+
+    torch.Tensor.pin_memory = lambda self, *a, **k: self  # no CUDA driver here; changes no decision
+    model = random_model("tiny")
+    cfg = model.config
+    per_tok = 2 * cfg.num_hidden_layers * cfg.num_key_value_heads * (cfg.hidden_size // cfg.num_attention_heads) * 4
+    gpu_budget, cpu_budget = per_tok * 90, per_tok * 70
+    gaps = []
+    fwd = type(model).forward
+
+    def spy(self, *a, **kw):
+        out = fwd(self, *a, **kw)
+        top = out.logits[0, -1].float().topk(2).values
+        gaps.append(float(top[0] - top[1]))
+        return out
+
+    type(model).forward = spy
+    try:
+        eng = Engine(model, BlockStore(gpu_budget, cpu_budget_bytes=cpu_budget))
+        app = ts.build_app(model, StubTokenizer(cfg.vocab_size), eng, eos_ids={cfg.vocab_size - 1})
+        client = TestClient(app)
+        responses = []
+        for prefix, docs, suffix, tenant, max_tokens, ratio, policy in SERVER_REQUESTS:
+            r = client.post("/v1/completions", json=dict(prefix=prefix, documents=docs, suffix=suffix, tenant=tenant,
+                                                         max_tokens=max_tokens, recompute_ratio=ratio, policy=policy))
+            assert r.status_code == 200, r.text
+            body = r.json()
+            for k in ("ttft_ms", "total_ms"):
+                body["tread"].pop(k)
+            responses.append(body)
+        metrics = client.get("/metrics").json()
+        for k in ("ttft_ms_sum", "ttft_ms_mean"):
+            metrics.pop(k)
+    finally:
+        type(model).forward = fwd
+    np.savez_compressed(os.path.join(HERE, "server.npz"), responses=np.array(json.dumps(responses)),
+                        metrics=np.array(json.dumps(metrics)), gpu_budget=np.int64(gpu_budget),
+                        cpu_budget=np.int64(cpu_budget), min_top2_gap=np.float64(min(gaps)))
+
+
 ALL = ["rope", "deviation", "attention", "store", "engine_tiny", "engine_cfg1", "engine_bf16_tiny",
-       "engine_bf16_7b3l", "store_engine_bf16"]
+       "engine_bf16_7b3l", "store_engine_bf16", "server"]
 
 
 def main():

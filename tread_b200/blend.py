@@ -92,10 +92,10 @@ def _deviation_pass(net, ctx_ids, K, V, all_c, inplace, extra, budget):
         pos = torch.cat([all_c, extra[1]])
     h = net.layer(0, h, pos, K0, V0)
     hc = h[:n]
-    qkv1 = net.qkv(1, hc)
+    kv1 = net.kv(1, hc)  # k/v columns only
     k1 = torch.empty(net.Hkv, n, net.D, dtype=hc.dtype, device=hc.device)
     v1 = torch.empty_like(k1)
-    kernels.rope_rows(qkv1, all_c, net.Hq, net.Hkv, net.D, None, k1, v1, net.inv_freq, net.attn_scaling, net.err,
+    kernels.rope_rows(kv1, all_c, 0, net.Hkv, net.D, None, k1, v1, net.inv_freq, net.attn_scaling, net.err,
                       kv_by_row=True)
     dev, sel_idx, S = net.deviation_select(k1, v1, K[1], V[1], all_c, budget)
     return dev, sel_idx, S, hc, K0, V0, (h[n:] if extra is not None else None)

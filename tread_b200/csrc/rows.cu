@@ -104,7 +104,9 @@ extern "C" int tread_rope_rows(const void* qkv, int64_t ld_qkv, const int64_t* p
   TREAD_CHECK_ARG(R >= 0, "rope_rows: R < 0");
   if (R == 0) return TREAD_OK;
   TREAD_CHECK_ARG(qkv && pos && K_cache && V_cache && inv_freq, "rope_rows: null pointer");
-  TREAD_CHECK_ARG(Hq > 0 && Hkv > 0 && Hq % Hkv == 0, "rope_rows: bad heads Hq=%d Hkv=%d", Hq, Hkv);
+  // Hq == 0 (no q output): the rows hold only [k heads | v heads]
+  TREAD_CHECK_ARG(Hkv > 0 && (Hq > 0 ? Hq % Hkv == 0 : (Hq == 0 && q_out == nullptr)),
+                  "rope_rows: bad heads Hq=%d Hkv=%d (Hq = 0 needs q_out == NULL)", Hq, Hkv);
   TREAD_CHECK_ARG(D >= 2 && D % 2 == 0 && D / 2 <= kMaxHalf, "rope_rows: bad head_dim %d", D);
   TREAD_CHECK_ARG(ld_qkv >= (int64_t)(Hq + 2 * Hkv) * D, "rope_rows: ld_qkv %lld too small", (long long)ld_qkv);
   TREAD_CHECK_ARG(T_cache > 0 && cache_stride_head >= T_cache * D, "rope_rows: bad cache geometry");

@@ -298,7 +298,8 @@ def rope_rows(qkv, pos, Hq, Hkv, D, q_out, K, V, inv_freq, attn_scaling=1.0, err
     """Rotate the rows' q heads into q_out [R, Hq, D] (skipped if q_out is None) and splice their
     rotated k / plain v into the layer cache K/V at `pos` (tread/blend.py:82-90,106); with
     kv_by_row, row r's k/v go to cache row r instead (dense [Hkv, R, D] outputs).
-    qkv: [R, >= (Hq+2Hkv)*D] with unit column stride."""
+    qkv: [R, >= (Hq+2Hkv)*D] with unit column stride; with q_out None and Hq = 0 the rows hold
+    only [k heads | v heads]."""
     C.require_cuda(qkv, "qkv")
     K = _layer_cache(K, "K")
     V = _layer_cache(V, "V")

@@ -82,6 +82,14 @@ class Qwen2Rows:
         p = self.layers[l]
         return torch.addmm(p["bqkv"], self.rmsnorm(h, p["ln1"], p["ln1_eps"]), p["wqkv"].t())
 
+    def kv(self, l, h):
+        """Only the k and v columns of layer l's projection, [R, 2 * Hkv * D]: the deviation
+        selector's fresh layer-1 rows (tread/blend.py:127-128) need no queries, so their GEMM
+        skips the Hq * D query columns."""
+        p = self.layers[l]
+        nq = self.Hq * self.D
+        return torch.addmm(p["bqkv"][nq:], self.rmsnorm(h, p["ln1"], p["ln1_eps"]), p["wqkv"][nq:].t())
+
     def layer(self, l, h, pos, K, V, qkv=None):
         """h: [R, hidden] rows at positions pos (int64 [R]); K, V: layer-l caches [1, Hkv, T, D]
         (or [Hkv, T, D]); the rows' k/v are written into them. Returns the new residual rows

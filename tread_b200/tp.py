@@ -168,27 +168,51 @@ class TPQwen2Rows(Qwen2Rows):
             return cls(cfg, _random_layers(cfg, seed, device, dtype), embed, norm_w, cfg.rms_norm_eps, lm_head,
                        group, dtype, device)
 
-    def _row_parallel(self, a, w, h):
+    # -- collective timing (off unless a caller sets `collective_events` to a list) ---------------
+    collective_events = None
+
+    def _timed(self, name, fn):
+        """Run the collective `fn`; with collective timing on, bracket it with CUDA events on the
+        current stream (its device time on this rank, waiting for the peers included)."""
+        if self.collective_events is None:
+            return fn()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        out = fn()
+        b.record()
+        self.collective_events.append((name, a, b))
+        return out
+
+    def collective_ms(self):
+        """Milliseconds per collective kind since collective timing was switched on (synchronises)."""
+        torch.cuda.synchronize(self.device)
+        tot = {}
+        for name, a, b in self.collective_events or ():
+            tot[name] = tot.get(name, 0.0) + a.elapsed_time(b)
+        return tot
+
+    def _row_parallel(self, a, w, h, name):
         """h + sum over ranks of a_r @ w_r^T (rank 0 folds the residual into its product)."""
         out = torch.addmm(h, a, w.t()) if self.rank == 0 else a @ w.t()
         if self.world > 1:
-            dist.all_reduce(out, group=self.group)
+            self._timed(name, lambda: dist.all_reduce(out, group=self.group))
         return out
 
     def layer_tail(self, l, h, o):
         """Row-parallel o_proj and down_proj with their all-reduces; returns the new residual rows
         (a new tensor, identical on every rank)."""
         p = self.layers[l]
-        h = self._row_parallel(o, p["wo"], h)
+        h = self._row_parallel(o, p["wo"], h, "o_proj_allreduce")
         x = self.rmsnorm(h, p["ln2"], p["ln2_eps"])
         a = kernels.silu_mul(x @ p["wgu"].t())
-        return self._row_parallel(a, p["wd"], h)
+        return self._row_parallel(a, p["wd"], h, "down_proj_allreduce")
 
     def deviation_select(self, k1, v1, K1, V1, cand_pos, budget):
         """Per-head norms of this rank's heads, all-gathered, then the fixed-order head sum and
         the top-`budget` selection on every rank (same result everywhere)."""
         norms = kernels.deviation_head_norms(k1, v1, K1, V1, cand_pos)
-        return kernels.select_head_norms(gather_head_norms(norms, self.group), cand_pos, budget)
+        allnorms = self._timed("head_norms_allgather", lambda: gather_head_norms(norms, self.group))
+        return kernels.select_head_norms(allnorms, cand_pos, budget)
 
     def check_errors(self):
         """Raise on every rank if a kernel on any rank flagged an error (row kernels' error word
