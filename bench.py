@@ -693,10 +693,10 @@ def run_ttft_tp(args, dev, world, rank, arch, prefix_len, ndocs, doc_len, q_len)
         if world > 1:
             # one more request of the same kind with every collective bracketed by CUDA events
             # (kept out of the timed requests above): device ms per collective kind, max over ranks
-            order = [docs[i] for i in torch.randperm(ndocs, generator=pg).tolist()]
+            order_c = [docs[i] for i in torch.randperm(ndocs, generator=pg).tolist()]
             net.collective_events = []
             barrier(world)
-            logits_c, cache, _ = eng.prefill(prefix, order, query, ratio=ratio)
+            logits_c, cache, _ = eng.prefill(prefix, order_c, query, ratio=ratio)
             int(logits_c.argmax().item())
             del cache
             cms = net.collective_ms()

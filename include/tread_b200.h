@@ -191,14 +191,26 @@ int tread_rope_rows(const void* qkv, int64_t ld_qkv, const int64_t* pos, int R, 
  * (tread/engine.py:131-132). q, out: [R, Hq, D]; K/V: one layer's [Hkv, T_cache, D] at head
  * stride cache_stride_head; softmax in fp32 with scores scaled by sm_scale. Positions outside
  * [0, T_cache) skip their row and set bit 1 of *err_flag (may be NULL).
- * bf16 / fp16 with D == 128 run on the tcgen05 tensor-core kernel (TMA-fed, S and O in TMEM);
- * a bounded mbarrier wait that gives up sets bit 2 of *err_flag. flags bit 0 forces the
- * CUDA-core kernel (used for fp32 and the other head dims).
+ * bf16 / fp16 with D == 128 run on the tcgen05 tensor-core kernel (TMA-fed, S, P and O in
+ * TMEM). A bounded mbarrier wait that gives up sets bit 2 of *err_flag. flags bit 0 forces the
+ * CUDA-core kernel (used for fp32 and the other head dims); bit 1 forces the stream-K schedule
+ * below whatever the tile count (otherwise it runs only when the 128-row tiles of all heads do not
+ * fill one wave of SMs).
+ *
+ * workspace (device, 256-byte aligned, tread_attn_rows_workspace_bytes() of it, zero-filled once by
+ * the caller; may be NULL): with it, the tensor-core kernel can run one CTA per SM over equal
+ * shares of all key blocks of all row tiles (stream-K), a tile split between CTAs being merged
+ * from partial results kept there; the kernel returns its counters to zero, except after an error
+ * of bit 2, when the caller must zero the workspace again. Without it each CTA runs one whole
+ * 128-row tile. Calls that share a workspace must be stream-ordered.
  */
 #define TREAD_ATTN_FORCE_CUDA_CORES 1
+#define TREAD_ATTN_FORCE_STREAM_K 2
+size_t tread_attn_rows_workspace_bytes(void);
 int tread_attn_rows(const void* q, const void* K_cache, const void* V_cache, int64_t cache_stride_head,
                     int64_t T_cache, const int64_t* q_pos, int R, int Hq, int Hkv, int D, float sm_scale,
-                    void* out, int dtype, int flags, void* err_flag, tread_stream_t stream);
+                    void* out, int dtype, int flags, void* err_flag, void* workspace,
+                    size_t workspace_bytes, tread_stream_t stream);
 
 /*
  * Fused RMSNorm over rows: y[r] = to_dtype(w * to_dtype(x[r] * rsqrt(mean(x[r]^2) + eps))), fp32

@@ -162,15 +162,17 @@ def test_rope_rows_rejects_bad_arguments(over, needle):
 
 def _attn_call(**over):
     a = dict(q=256, K=256, V=256, csh=128 * 16, T=16, pos=256, R=3, Hq=4, Hkv=2, D=128, scale=0.1, out=256,
-             dtype=C.TREAD_BF16, flags=0)
+             dtype=C.TREAD_BF16, flags=0, ws=None, ws_bytes=0)
     a.update(over)
     return C.lib().tread_attn_rows(a["q"], a["K"], a["V"], a["csh"], a["T"], a["pos"], a["R"], a["Hq"], a["Hkv"],
-                                   a["D"], a["scale"], a["out"], a["dtype"], a["flags"], None, None)
+                                   a["D"], a["scale"], a["out"], a["dtype"], a["flags"], None, a["ws"],
+                                   a["ws_bytes"], None)
 
 
 @pytest.mark.parametrize("over,needle", [
     (dict(R=-1), "R < 0"), (dict(Hq=3), "heads"), (dict(Hq=34, Hkv=2), "heads"), (dict(D=96), "head_dim"),
-    (dict(csh=10), "cache geometry"), (dict(dtype=9), "dtype"), (dict(flags=2), "flags"), (dict(out=None), "null"),
+    (dict(csh=10), "cache geometry"), (dict(dtype=9), "dtype"), (dict(flags=4), "flags"), (dict(out=None), "null"),
+    (dict(ws=264, ws_bytes=1 << 20), "workspace"),
 ])
 def test_attn_rows_rejects_bad_arguments(over, needle):
     assert _attn_call(**over) == 1

@@ -305,6 +305,26 @@ def _sdpa_ref(q, K, V, pos):
     return o.transpose(0, 1)
 
 
+# variants of the tensor-core kernel: the default choice, the stream-K schedule forced, one whole
+# row tile per CTA (no workspace)
+VARIANTS = {"default": {}, "stream_k": dict(stream_k=True), "whole_tiles": dict(workspace=False)}
+
+
+def _check_attention(cuda, dtype, q, K, V, pos, variants=VARIANTS):
+    R = q.shape[0]
+    err = torch.zeros(4, dtype=torch.int32, device=cuda)
+    o_cc = kernels.attn_rows(q, K, V, pos, err=err, cuda_cores=True)
+    idx = torch.arange(0, R, max(1, R // 200), device=cuda)
+    ref = _sdpa_ref(q[idx], K, V, pos[idx])
+    tol = 2e-2 if dtype == torch.bfloat16 else 4e-3
+    for name in variants:
+        o = kernels.attn_rows(q, K, V, pos, err=err, **VARIANTS[name])
+        torch.cuda.synchronize()
+        assert err.max().item() == 0, name
+        torch.testing.assert_close(o[idx].float(), ref, rtol=0, atol=tol, msg=lambda m: f"{name}: {m}")
+        torch.testing.assert_close(o.float(), o_cc.float(), rtol=0, atol=tol, msg=lambda m: f"{name}: {m}")
+
+
 @pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
 # the 4096-row case fills more than four waves of 148 SMs (896 tiles)
 @pytest.mark.parametrize("R,Hq,Hkv,T", [(17, 7, 1, 150), (300, 14, 2, 1000), (1651, 28, 4, 8256), (129, 8, 8, 129),
@@ -318,16 +338,56 @@ def test_tensor_core_attention_matches_fp32_reference(cuda, dtype, R, Hq, Hkv, T
     pos = torch.sort(torch.randperm(T, device=cuda, generator=gen)[:R]).values
     if R > 64:
         pos[-16:] = torch.arange(T - 16, T, device=cuda)  # query rows at the end of the cache
-    err = torch.zeros(4, dtype=torch.int32, device=cuda)
-    o = kernels.attn_rows(q, K, V, pos, err=err)
-    o_cc = kernels.attn_rows(q, K, V, pos, err=err, cuda_cores=True)
-    torch.cuda.synchronize()
-    assert err.max().item() == 0
-    idx = torch.arange(0, R, max(1, R // 200), device=cuda)
-    ref = _sdpa_ref(q[idx], K, V, pos[idx])
-    tol = 2e-2 if dtype == torch.bfloat16 else 4e-3
-    torch.testing.assert_close(o[idx].float(), ref, rtol=0, atol=tol)
-    torch.testing.assert_close(o.float(), o_cc.float(), rtol=0, atol=tol)
+    _check_attention(cuda, dtype, q, K, V, pos)
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+@pytest.mark.parametrize("case", ["causal_prefill", "unsorted", "query_only", "one_row"])
+def test_tensor_core_attention_schedules(cuda, dtype, case):
+    """Shapes that stress the stream-K split and merge: a causal prefill of 8000 rows (the deviation
+    pass's layer 0: tiles of 1..63 key blocks), rows in random order (a tile's length is its latest
+    row), 64 query rows only (14 pairs split over every SM), a single row."""
+    gen = torch.Generator(device=cuda).manual_seed(7)
+    Hq, Hkv, D = 28, 4, 128
+    if case == "causal_prefill":
+        T = 8064
+        pos = torch.arange(8000, device=cuda) + 64
+    elif case == "unsorted":
+        T = 5000
+        pos = torch.randperm(T, device=cuda, generator=gen)[:777]
+    elif case == "query_only":
+        T = 8320
+        pos = torch.arange(T - 64, T, device=cuda)
+    else:
+        T = 3000
+        pos = torch.tensor([2999], device=cuda)
+    R = len(pos)
+    q = torch.randn(R, Hq, D, device=cuda, generator=gen).to(dtype)
+    K = torch.randn(Hkv, T, D, device=cuda, generator=gen).to(dtype)
+    V = torch.randn(Hkv, T, D, device=cuda, generator=gen).to(dtype)
+    _check_attention(cuda, dtype, q, K, V, pos)
+
+
+def test_tensor_core_attention_flags_out_of_range_positions(cuda):
+    """A position past the cache end: the row is computed as position 0 and bit 1 of the error
+    word is set; the other rows are unaffected."""
+    gen = torch.Generator(device=cuda).manual_seed(3)
+    R, Hq, Hkv, D, T = 300, 14, 2, 128, 1000
+    q = torch.randn(R, Hq, D, device=cuda, generator=gen).to(torch.bfloat16)
+    K = torch.randn(Hkv, T, D, device=cuda, generator=gen).to(torch.bfloat16)
+    V = torch.randn(Hkv, T, D, device=cuda, generator=gen).to(torch.bfloat16)
+    pos = torch.sort(torch.randperm(T, device=cuda, generator=gen)[:R]).values
+    bad = pos.clone()
+    bad[5] = T + 3
+    for kw in ({}, dict(workspace=False)):
+        err = torch.zeros(4, dtype=torch.int32, device=cuda)
+        o = kernels.attn_rows(q, K, V, bad, err=err, **kw)
+        torch.cuda.synchronize()
+        assert int(err[0].item()) & 2
+        good = torch.ones(R, dtype=torch.bool, device=cuda)
+        good[5] = False
+        ref = _sdpa_ref(q, K, V, pos)
+        torch.testing.assert_close(o[good].float(), ref[good], rtol=0, atol=2e-2)
 
 
 @pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
@@ -349,13 +409,14 @@ def test_tensor_core_attention_divergent_rescale(cuda, dtype):
     q, K, V = q.to(dtype), K.to(dtype), V.to(dtype)
     pos = torch.full((R,), T - 1, device=cuda, dtype=torch.int64)
     pos[::3] = torch.arange(0, R, 3, device=cuda) + 310  # some rows stop between the spikes
-    err = torch.zeros(4, dtype=torch.int32, device=cuda)
-    o = kernels.attn_rows(q, K, V, pos, err=err)
-    torch.cuda.synchronize()
-    assert err.max().item() == 0
     ref = _sdpa_ref(q, K, V, pos)
     tol = 2e-2 if dtype == torch.bfloat16 else 4e-3
-    torch.testing.assert_close(o.float(), ref, rtol=0, atol=tol)
+    for name, kw in VARIANTS.items():
+        err = torch.zeros(4, dtype=torch.int32, device=cuda)
+        o = kernels.attn_rows(q, K, V, pos, err=err, **kw)
+        torch.cuda.synchronize()
+        assert err.max().item() == 0, name
+        torch.testing.assert_close(o.float(), ref, rtol=0, atol=tol, msg=lambda m: f"{name}: {m}")
 
 
 @pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16, torch.float32])

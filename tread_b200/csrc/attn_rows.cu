@@ -126,7 +126,8 @@ int dispatch_d(int D, const void* q, const void* K, const void* V, long long c_s
 
 int attn_rows_dispatch(const void* q, const void* K, const void* V, long long c_sh, long long T_cache,
                        const int64_t* pos, int R, int Hq, int Hkv, int D, float sm_scale, void* out, int dtype,
-                       unsigned* err, cudaStream_t st, int force_simt);
+                       unsigned* err, void* ws, size_t ws_bytes, cudaStream_t st, int flags);
+size_t attn_tc_workspace_bytes();
 
 // CUDA-core recompute attention (all dtypes); the tensor-core path calls back into it for
 // shapes it does not cover.
@@ -143,9 +144,12 @@ int attn_rows_simt(const void* q, const void* K, const void* V, long long c_sh, 
 
 }  // namespace tread
 
+extern "C" size_t tread_attn_rows_workspace_bytes(void) { return tread::attn_tc_workspace_bytes(); }
+
 extern "C" int tread_attn_rows(const void* q, const void* K_cache, const void* V_cache, int64_t cache_stride_head,
                                int64_t T_cache, const int64_t* q_pos, int R, int Hq, int Hkv, int D, float sm_scale,
-                               void* out, int dtype, int flags, void* err_flag, tread_stream_t stream) {
+                               void* out, int dtype, int flags, void* err_flag, void* workspace,
+                               size_t workspace_bytes, tread_stream_t stream) {
   using namespace tread;
   TREAD_CHECK_ARG(R >= 0, "attn_rows: R < 0");
   if (R == 0) return TREAD_OK;
@@ -156,8 +160,10 @@ extern "C" int tread_attn_rows(const void* q, const void* K_cache, const void* V
   TREAD_CHECK_ARG(T_cache > 0 && cache_stride_head >= T_cache * D, "attn_rows: bad cache geometry");
   TREAD_CHECK_ARG(R <= 2147483647 && Hkv <= 65535, "attn_rows: grid too large");
   TREAD_CHECK_ARG(dtype_size(dtype) != 0, "attn_rows: unknown dtype %d", dtype);
-  TREAD_CHECK_ARG((flags & ~1) == 0, "attn_rows: unknown flags %#x", flags);
+  TREAD_CHECK_ARG((flags & ~3) == 0, "attn_rows: unknown flags %#x", flags);
+  TREAD_CHECK_ARG(workspace == nullptr || (reinterpret_cast<uintptr_t>(workspace) & 255u) == 0,
+                  "attn_rows: workspace not 256-byte aligned");
   return attn_rows_dispatch(q, K_cache, V_cache, cache_stride_head, T_cache, q_pos, R, Hq, Hkv, D, sm_scale, out,
-                            dtype, static_cast<unsigned*>(err_flag), reinterpret_cast<cudaStream_t>(stream),
-                            flags & 1);
+                            dtype, static_cast<unsigned*>(err_flag), workspace, workspace ? workspace_bytes : 0,
+                            reinterpret_cast<cudaStream_t>(stream), flags);
 }

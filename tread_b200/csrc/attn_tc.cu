@@ -1,583 +1,54 @@
 // Recompute attention on the 5th-generation tensor cores (tcgen05 + TMEM + TMA), sm_100a.
 //
 // Same contract as the CUDA-core path in attn_rows.cu (tread/blend.py:76,110 and the query
-// forward of tread/engine.py:131-132): row r of head h attends to every cache key at a
-// position <= pos[r] of KV head h / (Hq/Hkv). This path covers bf16/fp16 with head_dim 128.
+// forward of tread/engine.py:131-132): row r of head h attends to every cache key at a position
+// <= pos[r] of KV head h / (Hq/Hkv). This path covers bf16/fp16 with head_dim 128.
 //
-// One CTA owns a tile of 128 consecutive rows of one query head; the heaviest tiles (latest
-// positions, longest key ranges) are scheduled first. Roles and pipeline:
-//   - loader (lane 0 of warp 9): TMA (128-byte swizzle) loads the Q tile once and 128-key K and V
-//     tiles into separate 2-stage rings (two steps ahead of the MMAs that read them) straight
-//     from the [R, Hq, D] queries and the [Hkv, T, D] cache, refilling a stage when the MMA that
-//     read it commits to that stage's "free" barrier;
-//   - MMA issuer (lane 0 of warp 8): issues S_j = Q K_j^T (8 x tcgen05.mma kind::f16,
-//     M=N=K=128, operands in shared memory) into one of two TMEM S buffers, so the MMA of step
-//     j+1 runs while the rows are still in the softmax of step j, and PV_j as two K=64 halves,
-//     O_h += P_j[:, half h] V_j[half h, :], with P read from TMEM;
-//   - softmax (warps 0-7; a row = a TMEM lane, its 128 key columns split into two halves, one
-//     per warp): reads its half of S once with tcgen05.ld, masks keys past the row's position
-//     (only on tiles that reach it), keeps the half's own running max and sum in the exp2 domain
-//     (ex2.approx on the MUFU pipe, which stays below saturation), rescales the half's O
-//     in TMEM only when its max grows by more than 8 (a stale max is exact since 1/l uses the
-//     same max; a warp rescales together because tcgen05.ld/st are warp-collective), and writes
-//     P (bf16/fp16 pairs) with tcgen05.st over the S columns it has just read. The halves never
-//     wait for each other: they are merged once, in the epilogue, by their maxima;
-//   - mbarriers hand off K/V stages, S buffers, P and PV completion between the roles; QK(j+2)
-//     reuses S buffer j%2 after PV(j) has read the P in it.
-// TMEM: two 128-column S buffers + one 128-column O accumulator per key half (512 allocated; one
-// CTA per SM by its shared memory). Every wait is bounded in wall time and aborts the whole CTA
-// through a shared flag; an aborted CTA records bit 2 in *err, lets issued copies and MMAs land,
-// frees its TMEM and returns.
+// Work items and schedule. An item is a tile of 128 consecutive rows of one query head; it takes
+// n = (latest position among its rows) / 128 + 1 key blocks ("steps"). With a workspace, all
+// items' steps are laid end to end (items of one KV head together, for L2 reuse of its K/V) and
+// cut into one equal contiguous segment per CTA, one CTA per SM (stream-K): a CTA runs the pieces
+// of items in its segment one after another, and an item cut between CTAs leaves partial results
+// (unnormalised O, running max m and sum l per row) in the workspace; after its last piece a CTA
+// counts its (at most two) partial pieces in, and the one that completes an item (an atomic
+// count per item, no waiting) merges its partials:
+//     O = sum_k O_k 2^(m_k - M) / sum_k l_k 2^(m_k - M),  M = max_k m_k.
+// The schedule is used when the tiles do not fill one wave of SMs (the query rows alone); with
+// more tiles, or without a workspace, every CTA runs one whole tile, latest rows first (the
+// measured trade-off is at the launch site).
+//
+// Roles and pipeline per CTA:
+//   - loader (lane 0 of warp 9): TMA (128-byte swizzle) loads each piece's Q tile and 128-key K
+//     and V tiles into separate 2-stage rings, refilling a stage when the MMA that read it commits
+//     to that stage's "free" barrier; the next piece's Q loads once the last QK of the current
+//     piece has read the old one;
+//   - MMA issuer (warp 8; descriptors warp-uniform, one elected lane issues): S_g = Q K_g^T
+//     (8 x tcgen05.mma kind::f16, M=N=K=128, operands in shared memory) into TMEM S buffer g%2, so
+//     QK(g+1) runs while the rows are in the softmax of step g, and PV_g as two K=64 halves,
+//     O_h += P_g[:, half h] V_g[half h, :], with P read from TMEM;
+//   - softmax (warps 0-7; a row = a TMEM lane, its 128 key columns split into two halves, one per
+//     warp): reads its half of S once, masks keys past the row's position, keeps the half's own
+//     running max and sum in the exp2 domain (ex2.approx on MUFU), rescales the half's O in TMEM
+//     only when its max grows by more than 8 (a stale max is exact since 1/l uses the same max; a
+//     warp decides together because tcgen05.ld/st are warp-collective), and writes P over the S
+//     columns it has just read. The halves are merged once per piece, in the epilogue.
+// Steps are counted across a CTA's pieces, so the barrier phases (one barrier per S buffer and
+// ring stage: a parity wait never aliases) run on unchanged. TMEM: S buffers at columns 0 and
+// 128, the key halves' O accumulators at 256 and 384 (512 allocated; one CTA per SM). Every wait
+// is bounded in wall time and aborts the CTA through a shared flag; an aborted CTA records bit 2
+// in *err, lets issued copies and MMAs land, frees its TMEM and returns (the workspace's counters
+// must then be zeroed before the next call).
 #include <cuda.h>
 
 #include <mutex>
 #include <type_traits>
 
 #include "common.cuh"
+#include "tcgen05.cuh"
 
 namespace tread {
 
-int attn_rows_simt(const void* q, const void* K, const void* V, long long c_sh, long long T_cache, const int64_t* pos,
-                   int R, int Hq, int Hkv, int D, float sm_scale, void* out, int dtype, unsigned* err,
-                   cudaStream_t st);
-
-namespace {
-
-constexpr int kRows = 128;   // query rows per CTA (MMA M)
-constexpr int kKeys = 128;   // keys per step (MMA N of Q K^T, K of P V)
-constexpr int kD = 128;      // head_dim (MMA K of Q K^T, N of P V)
-constexpr int kBlock = 16384;  // one 128 x 64 bf16 swizzled block
-constexpr int kSmem = 10 * kBlock + 1024 + 256;
-constexpr unsigned long long kWaitNs = 1000000000ull;  // 1 s: legitimate waits here take microseconds
-constexpr unsigned long long kAbortWaitNs = 20000000ull;  // 20 ms per barrier phase on the abort path
-// TMEM columns: S buffers 0-127 and 128-255 (fp32; each column half also holds that half's P,
-// bf16/fp16 pairs, once read), O accumulators of key halves 0 and 1 at 256-383 and 384-511.
-constexpr uint32_t kTmemO = 256;
-
-__device__ __forceinline__ uint32_t smem_u32(const void* p) {
-  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
-}
-
-__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
-  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
-}
-
-__device__ __forceinline__ void mbar_expect_tx(uint64_t* bar, uint32_t bytes) {
-  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes)
-               : "memory");
-}
-
-__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t phase) {
-  uint32_t ok;
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t"
-      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
-      "selp.u32 %0, 1, 0, p;\n\t}"
-      : "=r"(ok)
-      : "r"(smem_u32(bar)), "r"(phase)
-      : "memory");
-  return ok != 0;
-}
-
-__device__ __forceinline__ unsigned long long global_ns() {
-  unsigned long long t;
-  asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
-  return t;
-}
-
-// Bounded wait: false if the phase did not complete within kWaitNs of wall time.
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t phase, unsigned long long limit_ns) {
-  if (mbar_try_wait(bar, phase)) return true;
-  const unsigned long long t0 = global_ns();
-  while (!mbar_try_wait(bar, phase))
-    if (global_ns() - t0 > limit_ns) return false;
-  return true;
-}
-
-__device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* map, uint64_t* bar, int x, int y, int z) {
-  asm volatile(
-      "cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4, %5}], [%2];" ::
-          "r"(smem_u32(dst)),
-      "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(x), "r"(y), "r"(z)
-      : "memory");
-}
-
-// Shared-memory matrix descriptor, 128-byte swizzle (tcgen05 format: version 1 at bit 46,
-// layout type 2 at bits 61-63), byte offsets encoded >> 4.
-__device__ __forceinline__ uint64_t sw128_desc(uint32_t addr, uint32_t lbo, uint32_t sbo) {
-  return (uint64_t)((addr >> 4) & 0x3FFFu) | ((uint64_t)((lbo >> 4) & 0x3FFFu) << 16) |
-         ((uint64_t)((sbo >> 4) & 0x3FFFu) << 32) | (1ull << 46) | (2ull << 61);
-}
-
-__device__ __forceinline__ void mma_f16(uint32_t tmem_d, uint64_t a, uint64_t b, uint32_t idesc, uint32_t acc) {
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t"
-      "setp.ne.b32 p, %4, 0;\n\t"
-      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
-      "l"(a), "l"(b), "r"(idesc), "r"(acc)
-      : "memory");
-}
-
-// Same with A (M x K, 16-bit elements packed two per 32-bit column, row = TMEM lane) in TMEM.
-__device__ __forceinline__ void mma_f16_ts(uint32_t tmem_d, uint32_t tmem_a, uint64_t b, uint32_t idesc,
-                                           uint32_t acc) {
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t"
-      "setp.ne.b32 p, %4, 0;\n\t"
-      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(tmem_d),
-      "r"(tmem_a), "l"(b), "r"(idesc), "r"(acc)
-      : "memory");
-}
-
-__device__ __forceinline__ void mma_commit(uint64_t* bar) {
-  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
-               : "memory");
-}
-
-__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
-__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
-
-// 32 consecutive fp32 TMEM columns of this thread's lane.
-__device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
-  uint32_t r[32];
-  asm volatile(
-      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
-      "%15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%32];"
-      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]),
-        "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]), "=r"(r[16]),
-        "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]),
-        "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
-      : "r"(taddr));
-  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-#pragma unroll
-  for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
-}
-
-// Same, without the wait: several loads can be in flight before one tcgen05.wait::ld.
-__device__ __forceinline__ void tmem_ld32_async(uint32_t taddr, uint32_t (&r)[32]) {
-  asm volatile(
-      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
-      "%15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%32];"
-      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]),
-        "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]), "=r"(r[16]),
-        "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]),
-        "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
-      : "r"(taddr)
-      : "memory");
-}
-
-__device__ __forceinline__ void tmem_st32(uint32_t taddr, const float (&v)[32]) {
-  asm volatile(
-      "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
-      "%15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31, %32};" ::"r"(taddr),
-      "r"(__float_as_uint(v[0])), "r"(__float_as_uint(v[1])), "r"(__float_as_uint(v[2])), "r"(__float_as_uint(v[3])),
-      "r"(__float_as_uint(v[4])), "r"(__float_as_uint(v[5])), "r"(__float_as_uint(v[6])), "r"(__float_as_uint(v[7])),
-      "r"(__float_as_uint(v[8])), "r"(__float_as_uint(v[9])), "r"(__float_as_uint(v[10])),
-      "r"(__float_as_uint(v[11])), "r"(__float_as_uint(v[12])), "r"(__float_as_uint(v[13])),
-      "r"(__float_as_uint(v[14])), "r"(__float_as_uint(v[15])), "r"(__float_as_uint(v[16])),
-      "r"(__float_as_uint(v[17])), "r"(__float_as_uint(v[18])), "r"(__float_as_uint(v[19])),
-      "r"(__float_as_uint(v[20])), "r"(__float_as_uint(v[21])), "r"(__float_as_uint(v[22])),
-      "r"(__float_as_uint(v[23])), "r"(__float_as_uint(v[24])), "r"(__float_as_uint(v[25])),
-      "r"(__float_as_uint(v[26])), "r"(__float_as_uint(v[27])), "r"(__float_as_uint(v[28])),
-      "r"(__float_as_uint(v[29])), "r"(__float_as_uint(v[30])), "r"(__float_as_uint(v[31]))
-      : "memory");
-}
-
-__device__ __forceinline__ void tmem_st32u(uint32_t taddr, const uint32_t (&v)[32]) {
-  asm volatile(
-      "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
-      "%15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31, %32};" ::"r"(taddr),
-      "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7]), "r"(v[8]), "r"(v[9]),
-      "r"(v[10]), "r"(v[11]), "r"(v[12]), "r"(v[13]), "r"(v[14]), "r"(v[15]), "r"(v[16]), "r"(v[17]), "r"(v[18]),
-      "r"(v[19]), "r"(v[20]), "r"(v[21]), "r"(v[22]), "r"(v[23]), "r"(v[24]), "r"(v[25]), "r"(v[26]), "r"(v[27]),
-      "r"(v[28]), "r"(v[29]), "r"(v[30]), "r"(v[31])
-      : "memory");
-}
-
-template <typename T>
-__device__ __forceinline__ uint32_t pack2(float a, float b);
-template <>
-__device__ __forceinline__ uint32_t pack2<__nv_bfloat16>(float a, float b) {
-  __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
-  return *reinterpret_cast<uint32_t*>(&h);
-}
-template <>
-__device__ __forceinline__ uint32_t pack2<__half>(float a, float b) {
-  __half2 h = __floats2half2_rn(a, b);
-  return *reinterpret_cast<uint32_t*>(&h);
-}
-
-// Instruction descriptor, kind::f16: fp32 accumulate (bit 4), A/B format (bits 7-9, 10-12:
-// 0 = f16, 1 = bf16), B major (bit 16: 0 = K, 1 = MN), N >> 3 (bits 17-22), M >> 4 (bits 24-28).
-__host__ __device__ constexpr uint32_t idesc_f16(uint32_t fmt, uint32_t b_mn_major, uint32_t M, uint32_t N) {
-  return (1u << 4) | (fmt << 7) | (fmt << 10) | (b_mn_major << 16) | ((N >> 3) << 17) | ((M >> 4) << 24);
-}
-
-// Roles: warps 0-7 run the softmax: warp w covers TMEM lanes (rows) 32*(w%4).. and S/O columns
-// 64*(w/4).. of its row quadrant, so every row is shared by two warps that exchange their partial
-// max through shared memory; lane 0 of warp 8 issues every tcgen05.mma; lane 0 of warp 9 issues
-// every TMA load, waiting only on the "stage free" barriers the MMAs commit, so loads never hold
-// up MMA issue.
-constexpr int kWarpsPerQuad = 2;
-constexpr int kSoftWarps = 4 * kWarpsPerQuad;
-constexpr int kColsPerWarp = kKeys / kWarpsPerQuad;  // 64
-constexpr int kMmaWarp = kSoftWarps, kLoadWarp = kSoftWarps + 1;
-constexpr int kThreadsTC = (kSoftWarps + 2) * 32;
-
-struct Waiter {
-  volatile int* abort;
-  // Bounded wait on an mbarrier phase; false if the CTA aborted or kWaitNs passed (then it aborts).
-  __device__ __forceinline__ bool operator()(uint64_t* bar, uint32_t parity) const {
-    if (mbar_try_wait(bar, parity)) return true;
-    const unsigned long long t0 = global_ns();
-    while (!mbar_try_wait(bar, parity)) {
-      if (*abort) return false;
-      if (global_ns() - t0 > kWaitNs) {
-        *abort = 1;
-        return false;
-      }
-    }
-    return true;
-  }
-};
-
-__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
-  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
-}
-
-// Barrier over the softmax warps that share a row quadrant (named barrier 1 + quadrant).
-__device__ __forceinline__ void quad_sync(int quadrant) {
-  asm volatile("bar.sync %0, %1;" ::"r"(1 + quadrant), "r"(kWarpsPerQuad * 32) : "memory");
-}
-
-__device__ __forceinline__ float ex2(float x) {
-  float y;
-  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
-  return y;
-}
-
-// Packed two-wide fp32 arithmetic of sm_100 (one issue slot for two lanes' worth of work): the
-// softmax is issue-bound, so halving its FMAs and adds shortens each step.
-__device__ __forceinline__ float2 ffma2(float2 a, float2 b, float2 c) {
-  float2 d;
-  asm("{\n\t.reg .b64 ra, rb, rc, rd;\n\t"
-      "mov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\tmov.b64 rc, {%6, %7};\n\t"
-      "fma.rn.f32x2 rd, ra, rb, rc;\n\tmov.b64 {%0, %1}, rd;\n\t}"
-      : "=f"(d.x), "=f"(d.y)
-      : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y), "f"(c.x), "f"(c.y));
-  return d;
-}
-
-__device__ __forceinline__ float2 fadd2(float2 a, float2 b) {
-  float2 d;
-  asm("{\n\t.reg .b64 ra, rb, rd;\n\t"
-      "mov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\t"
-      "add.rn.f32x2 rd, ra, rb;\n\tmov.b64 {%0, %1}, rd;\n\t}"
-      : "=f"(d.x), "=f"(d.y)
-      : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y));
-  return d;
-}
-
-__device__ __forceinline__ float fmax3(float a, float b, float c) {
-  float d;
-  asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
-  return d;
-}
-
-template <typename T>
-__global__ void __launch_bounds__(kThreadsTC, 1)
-    attn_rows_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
-                        const __grid_constant__ CUtensorMap tm_v, const int64_t* __restrict__ pos, int R, int Hq,
-                        int G, long long T_cache, float scale_log2, T* __restrict__ out, unsigned* err) {
-  extern __shared__ __align__(1024) unsigned char smem_raw[];
-  unsigned char* smem =
-      reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  unsigned char* sQ = smem;               // 2 blocks: d 0-63, d 64-127
-  unsigned char* sK = smem + 2 * kBlock;  // 2 stages x 2 blocks
-  unsigned char* sV = smem + 6 * kBlock;  // 2 stages x 2 blocks
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + 10 * kBlock);
-  uint64_t* q_full = bars + 0;
-  uint64_t* k_full = bars + 1;   // [2] K stage loaded
-  uint64_t* v_full = bars + 3;   // [2] V stage loaded
-  uint64_t* s_full = bars + 5;   // [2] S buffer written by QK
-  // bars 7-8: unused
-  uint64_t* p_full = bars + 9;   // [2] P of S buffer b written by the softmax
-  uint64_t* pv_done = bars + 11; // [2] PV of S buffer b's P complete (buffer reusable, O stable)
-  uint64_t* k_free = bars + 13;  // [2] K stage read by its QK
-  uint64_t* v_free = bars + 15;  // [2] V stage read by its PV
-  constexpr int kNumBars = 17;
-  uint32_t* s_tmem = reinterpret_cast<uint32_t*>(bars + kNumBars);
-  int* s_abort = reinterpret_cast<int*>(bars + kNumBars + 1);
-  __shared__ int s_wmax[4];
-  __shared__ float s_part[2][kWarpsPerQuad][kRows];  // [step parity][column part][row]: max / final sum
-
-  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int quad = warp & 3, part = warp >> 2;
-  const int h = blockIdx.x, g = h / G;
-  const int tile = gridDim.y - 1 - blockIdx.y;  // latest rows (longest key ranges) start first
-  const int r0 = tile * kRows;
-  const int trow = quad * 32 + lane;  // row within the tile (= TMEM lane)
-  const int row = r0 + trow;
-  const bool soft = warp < kSoftWarps;
-  const bool live = soft && row < R;
-  long long p = live ? pos[row] : 0;
-  if (p < 0 || p >= T_cache) {
-    if (live && part == 0 && err) atomicOr(err, 2u);
-    p = 0;
-  }
-  if (warp < 4) {
-    const int wm = __reduce_max_sync(0xffffffffu, (unsigned)p);
-    if (lane == 0) s_wmax[warp] = wm;
-  }
-  if (warp == 0) {
-    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(s_tmem)),
-                 "r"(512)
-                 : "memory");
-    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
-  }
-  if (tid == 0) {
-    mbar_init(q_full, 1);
-    mbar_init(&k_full[0], 1);
-    mbar_init(&k_full[1], 1);
-    mbar_init(&v_full[0], 1);
-    mbar_init(&v_full[1], 1);
-    mbar_init(&s_full[0], 1);
-    mbar_init(&s_full[1], 1);
-    mbar_init(&p_full[0], kSoftWarps * 32);
-    mbar_init(&p_full[1], kSoftWarps * 32);
-    mbar_init(&pv_done[0], 1);
-    mbar_init(&pv_done[1], 1);
-    mbar_init(&k_free[0], 1);
-    mbar_init(&k_free[1], 1);
-    mbar_init(&v_free[0], 1);
-    mbar_init(&v_free[1], 1);
-    *s_abort = 0;
-    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
-  }
-  tc_fence_before();
-  __syncthreads();
-  tc_fence_after();
-  const uint32_t tmem = *s_tmem;
-  const int nsteps = max(max(s_wmax[0], s_wmax[1]), max(s_wmax[2], s_wmax[3])) / kKeys + 1;
-  // padding rows past R (output discarded) see every key, so they never take the masking path
-  if (soft && row >= R) p = (long long)nsteps * kKeys - 1;
-  const Waiter wait{s_abort};
-
-  if (warp == kLoadWarp) {
-    // ------------------------------------------------------------------ TMA loader (one lane)
-    // K and V have separate 2-stage rings; K(j+2) goes into its stage once QK(j) has read it and
-    // V(j+2) once PV(j) has, so copies run two steps ahead of the MMAs.
-    if (lane == 0) {
-      auto load_k = [&](int j) {
-        const int s = j & 1;
-        mbar_expect_tx(&k_full[s], 2 * kBlock);
-        tma_load_3d(sK + s * 2 * kBlock, &tm_k, &k_full[s], 0, j * kKeys, g);
-        tma_load_3d(sK + s * 2 * kBlock + kBlock, &tm_k, &k_full[s], 64, j * kKeys, g);
-      };
-      auto load_v = [&](int j) {
-        const int s = j & 1;
-        mbar_expect_tx(&v_full[s], 2 * kBlock);
-        tma_load_3d(sV + s * 2 * kBlock, &tm_v, &v_full[s], 0, j * kKeys, g);
-        tma_load_3d(sV + s * 2 * kBlock + kBlock, &tm_v, &v_full[s], 64, j * kKeys, g);
-      };
-      mbar_expect_tx(q_full, 2 * kBlock);
-      tma_load_3d(sQ, &tm_q, q_full, 0, h, r0);
-      tma_load_3d(sQ + kBlock, &tm_q, q_full, 64, h, r0);
-      for (int j = 0; j < nsteps && j < 2; ++j) {
-        load_k(j);
-        load_v(j);
-      }
-      for (int j = 0; j + 2 < nsteps; ++j) {
-        const int s = j & 1;
-        if (!wait(&k_free[s], (j >> 1) & 1)) break;
-        load_k(j + 2);
-        if (!wait(&v_free[s], (j >> 1) & 1)) break;
-        load_v(j + 2);
-      }
-    }
-  } else if (warp == kMmaWarp) {
-    // ------------------------------------------------------------------ MMA issuer (one lane)
-    if (lane == 0) {
-      constexpr uint32_t fmt = std::is_same<T, __nv_bfloat16>::value ? 1u : 0u;
-      constexpr uint32_t idesc_qk = idesc_f16(fmt, 0, kRows, kKeys);
-      constexpr uint32_t idesc_pv = idesc_f16(fmt, 1, kRows, kD);
-      const uint32_t aQ = smem_u32(sQ), aK = smem_u32(sK), aV = smem_u32(sV);
-      // PV(j): O_h += P_j[:, keys of half h] V_j[keys of half h, :] for h = 0, 1; P of half h sits
-      // in S buffer j%2 at columns 64*h .. 64*h+31 (packed pairs)
-      auto issue_pv = [&](int j) {
-        const int b = j & 1;
-        const uint32_t vbase = aV + b * 2 * kBlock;
-#pragma unroll
-        for (int k = 0; k < kKeys / 16; ++k)
-          mma_f16_ts(tmem + kTmemO + (k >> 2) * 128, tmem + b * kKeys + (k >> 2) * 64 + (k & 3) * 8,
-                     sw128_desc(vbase + k * 16 * 128, kBlock, 1024), idesc_pv, (j > 0 || (k & 3) > 0) ? 1u : 0u);
-        mma_commit(&pv_done[b]);
-        mma_commit(&v_free[b]);
-      };
-      bool ok = true;
-      for (int j = 0; j < nsteps && ok; ++j) {
-        const int s = j & 1;
-        // S buffer s holds P(j-2) until PV(j-2) has read it
-        ok = wait(&k_full[s], (j >> 1) & 1) && (j > 0 || wait(q_full, 0)) &&
-             (j < 2 || wait(&pv_done[s], ((j - 2) >> 1) & 1));
-        if (!ok) break;
-        tc_fence_after();
-        const uint32_t kbase = aK + s * 2 * kBlock;
-#pragma unroll
-        for (int k = 0; k < kD / 16; ++k) {
-          const uint32_t off = (k >> 2) * kBlock + (k & 3) * 32;
-          mma_f16(tmem + s * kKeys, sw128_desc(aQ + off, 16, 1024), sw128_desc(kbase + off, 16, 1024), idesc_qk,
-                  k > 0);
-        }
-        mma_commit(&s_full[s]);
-        mma_commit(&k_free[s]);
-        if (j >= 1) {
-          const int b = (j - 1) & 1;
-          ok = wait(&p_full[b], ((j - 1) >> 1) & 1) && wait(&v_full[b], ((j - 1) >> 1) & 1);
-          if (!ok) break;
-          tc_fence_after();
-          issue_pv(j - 1);
-        }
-      }
-      const int b = (nsteps - 1) & 1;
-      if (ok && wait(&p_full[b], ((nsteps - 1) >> 1) & 1) && wait(&v_full[b], ((nsteps - 1) >> 1) & 1)) {
-        tc_fence_after();
-        issue_pv(nsteps - 1);
-      }
-    }
-  } else {
-    // ------------------------------------------------------------------ softmax
-    // Each key half keeps its own running max, sum and O accumulator, so the two warps of a lane
-    // quadrant never wait for each other; the halves are merged once, in the epilogue.
-    const uint32_t lane_off = (uint32_t)(quad * 32) << 16;
-    const uint32_t col = part * kColsPerWarp;
-    const uint32_t tOh = tmem + kTmemO + part * 128;  // this half's O accumulator
-    float m = -INFINITY, l = 0.f;
-    bool ok = true;
-    for (int j = 0; j < nsteps; ++j) {
-      const int s = j & 1;
-      ok = __all_sync(0xffffffffu, wait(&s_full[s], (j >> 1) & 1));
-      if (!ok) break;
-      tc_fence_after();
-      float v[kColsPerWarp];
-      {
-        uint32_t r[kColsPerWarp / 32][32];
-#pragma unroll
-        for (int c = 0; c < kColsPerWarp / 32; ++c)
-          tmem_ld32_async(tmem + s * kKeys + col + c * 32 + lane_off, r[c]);
-        asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-#pragma unroll
-        for (int c = 0; c < kColsPerWarp / 32; ++c)
-#pragma unroll
-          for (int i = 0; i < 32; ++i) v[c * 32 + i] = __uint_as_float(r[c][i]);
-      }
-      const long long key0 = (long long)j * kKeys + col;
-      if (__any_sync(0xffffffffu, key0 + kColsPerWarp - 1 > p)) {
-        // keys i > lim of this half are past the row's position (one 32-bit compare each)
-        const int lim = (int)max(-1LL, min((long long)kColsPerWarp, p - key0));
-#pragma unroll
-        for (int i = 0; i < kColsPerWarp; ++i)
-          if (i > lim) v[i] = -INFINITY;
-      }
-      float m4[4] = {v[0], v[1], v[2], v[3]};  // four independent 3-input max chains
-#pragma unroll
-      for (int i = 4; i < kColsPerWarp; i += 2) m4[(i >> 1) & 3] = fmax3(m4[(i >> 1) & 3], v[i], v[i + 1]);
-      const float tmax = fmax3(m4[0], m4[1], fmaxf(m4[2], m4[3]));
-      const float m_new = fmaxf(m, tmax * scale_log2);  // -inf while every key of this half is masked
-      const bool rescale = j > 0 && m_new > m + 8.f;
-      float alpha = 1.f;
-      if (j == 0 || rescale) {
-        alpha = m == -INFINITY ? 0.f : ex2(m - m_new);
-        l *= alpha;
-        m = m_new;
-      }
-      const float mu = m == -INFINITY ? 0.f : m;  // all-masked half: exponentials of -inf give 0
-      uint32_t pk[kColsPerWarp / 2];
-      const float2 sc2 = make_float2(scale_log2, scale_log2), nm2 = make_float2(-mu, -mu);
-      float2 l2 = make_float2(0.f, 0.f);  // even / odd key sums
-#pragma unroll
-      for (int i = 0; i < kColsPerWarp; i += 2) {
-        const float2 x = ffma2(make_float2(v[i], v[i + 1]), sc2, nm2);
-        const float2 pp = make_float2(ex2(x.x), ex2(x.y));
-        l2 = fadd2(l2, pp);
-        pk[i / 2] = pack2<T>(pp.x, pp.y);
-      }
-      l += l2.x + l2.y;
-      // this half's O must be stable (PV(j-1) complete) to rescale it; tcgen05.ld/st are
-      // warp-collective, so the warp rescales together, other lanes by 1
-      if (__any_sync(0xffffffffu, rescale)) {
-        ok = __all_sync(0xffffffffu, wait(&pv_done[s ^ 1], ((j - 1) >> 1) & 1));
-        if (!ok) break;
-        tc_fence_after();
-#pragma unroll 1
-        for (int c = 0; c < kD / 32; ++c) {
-          float o[32];
-          tmem_ld32(tOh + lane_off + c * 32, o);
-#pragma unroll
-          for (int i = 0; i < 32; ++i) o[i] *= alpha;
-          tmem_st32(tOh + lane_off + c * 32, o);
-        }
-      }
-      // P over this warp's own S columns (already in registers): QK(j+2) waits for PV(j)
-      tmem_st32u(tmem + s * kKeys + part * 64 + lane_off, pk);
-      asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
-      tc_fence_before();
-      mbar_arrive(&p_full[s]);
-    }
-    if (ok) ok = __all_sync(0xffffffffu, wait(&pv_done[(nsteps - 1) & 1], ((nsteps - 1) >> 1) & 1));
-    if (ok) {
-      tc_fence_after();
-      // merge the halves: O = (O_0 2^(m_0 - M) + O_1 2^(m_1 - M)) / (l_0 2^(m_0 - M) + l_1 2^(m_1 - M))
-      s_part[0][part][trow] = m;
-      s_part[1][part][trow] = l;
-      quad_sync(quad);
-      const float m0 = s_part[0][0][trow], m1 = s_part[0][1][trow];
-      const float M = fmaxf(m0, m1);  // finite: key 0 is in half 0 and visible to every row
-      const float a0 = m0 == -INFINITY ? 0.f : ex2(m0 - M), a1 = m1 == -INFINITY ? 0.f : ex2(m1 - M);
-      const float inv = 1.f / (s_part[1][0][trow] * a0 + s_part[1][1][trow] * a1);
-      const float c0 = a0 * inv, c1 = a1 * inv;
-      T* orow = out + ((long long)row * Hq + h) * kD + col;
-#pragma unroll 1
-      for (int c = 0; c < kColsPerWarp / 32; ++c) {
-        float o0[32], o1[32];
-        tmem_ld32(tmem + kTmemO + col + lane_off + c * 32, o0);
-        tmem_ld32(tmem + kTmemO + 128 + col + lane_off + c * 32, o1);
-        if (live) {
-#pragma unroll
-          for (int i = 0; i < 32; i += 8) {
-            float w8[8];
-#pragma unroll
-            for (int e = 0; e < 8; ++e) w8[e] = fmaf(o0[i + e], c0, o1[i + e] * c1);
-            uint4 w = make_uint4(pack2<T>(w8[0], w8[1]), pack2<T>(w8[2], w8[3]), pack2<T>(w8[4], w8[5]),
-                                 pack2<T>(w8[6], w8[7]));
-            *reinterpret_cast<uint4*>(orow + c * 32 + i) = w;
-          }
-        }
-      }
-    }
-  }
-  tc_fence_before();
-  __syncthreads();
-  if (*s_abort && tid == 0) {
-    if (err) atomicOr(err, 4u);
-    // let copies and MMAs already issued land before the CTA's resources go away: each barrier
-    // an async unit arrives on gets a short bounded wait on both parities
-    for (int b = 0; b < 2; ++b)
-      for (int i = 0; i < kNumBars; ++i)
-        if (i != 7 && i != 8 && i != 9 && i != 10) mbar_wait(bars + i, b, kAbortWaitNs);
-  }
-  __syncthreads();
-  if (warp == 0) {
-    tc_fence_after();
-    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(512) : "memory");
-  }
-}
-
-// ---- host side: tensor maps -----------------------------------------------------------------
-
-using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
-                                   const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
-                                   CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+namespace tc {
 
 EncodeTiledFn encode_fn() {
   static EncodeTiledFn fn = nullptr;
@@ -592,7 +63,6 @@ EncodeTiledFn encode_fn() {
   return fn;
 }
 
-// 3-D bf16/fp16 map over (d, y, z) with element strides (1, sy, sz), box (64, by, bz), 128B swizzle.
 bool make_map(CUtensorMap* m, const void* base, CUtensorMapDataType dt, uint64_t nd, uint64_t ny, uint64_t nz,
               uint64_t sy, uint64_t sz, uint32_t by, uint32_t bz) {
   EncodeTiledFn fn = encode_fn();
@@ -606,9 +76,619 @@ bool make_map(CUtensorMap* m, const void* base, CUtensorMapDataType dt, uint64_t
             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
+}  // namespace tc
+
+int attn_rows_simt(const void* q, const void* K, const void* V, long long c_sh, long long T_cache, const int64_t* pos,
+                   int R, int Hq, int Hkv, int D, float sm_scale, void* out, int dtype, unsigned* err,
+                   cudaStream_t st);
+
+namespace {
+
+using namespace tc;
+
+constexpr int kRows = 128;   // query rows per item (MMA M)
+constexpr int kKeys = 128;   // keys per step (MMA N of Q K^T, K of P V)
+constexpr int kD = 128;      // head_dim (MMA K of Q K^T, N of P V)
+constexpr int kBlock = 16384;  // one 128 x 64 16-bit swizzled block
+constexpr int kMaxTiles = 2048;  // row tiles the stream-K plan tables hold (shared memory)
+// Q 2 buffers, K and V rings 2 stages, 2 blocks each (a buffer of Q lets the next piece's tile load
+// while the current piece runs)
+constexpr int kTilesBytes = 12 * kBlock;
+constexpr int kSmem = 1024 + kTilesBytes + 8 * kMaxTiles + 512;
+// Stream-K cost of an item's start and end (pipeline fill and drain, epilogue), in steps.
+constexpr int kPieceCost = 3;
+// TMEM columns: S buffers 0-127 and 128-255 (fp32; each column half also holds that half's P,
+// 16-bit pairs, once read), O accumulators of key halves 0 and 1 at 256-383 and 384-511.
+constexpr uint32_t kTmemO = 256;
+// workspace: one arrival counter per item (at most kMaxItems), then 2 partial slots per CTA:
+// O [128][128] fp32, m [128], l [128]
+constexpr int kMaxItems = 1 << 16;
+constexpr size_t kCounterBytes = (size_t)kMaxItems * 4;
+constexpr size_t kSlotBytes = (size_t)kRows * kD * 4 + 2 * kRows * 4;
+
+// Warps 0-7 run the softmax: warp w covers TMEM lanes (rows) 32*(w%4).. and S columns 64*(w/4)..
+// of its row quadrant; warp 8 issues every tcgen05.mma; lane 0 of warp 9 every TMA load.
+constexpr int kWarpsPerQuad = 2;
+constexpr int kSoftWarps = 4 * kWarpsPerQuad;
+constexpr int kColsPerWarp = kKeys / kWarpsPerQuad;  // 64
+constexpr int kMmaWarp = kSoftWarps, kLoadWarp = kSoftWarps + 1;
+constexpr int kThreadsTC = (kSoftWarps + 2) * 32;
+
+
+// Item p -> (query head, row tile): items of one KV group together, tile by tile, head by head.
+struct Item {
+  int head, tile, kvh;
+};
+__device__ __forceinline__ Item item_of(int p, int G, int ntiles) {
+  const int per_group = G * ntiles;
+  const int g = p / per_group, r = p - g * per_group;
+  const int t = r / G;
+  return Item{g * G + (r - t * G), t, g};
+}
+
+struct Piece {
+  int item, j0, j1, n_item;
+  bool first;  // first piece of this CTA's segment (workspace slot 2c, else 2c+1)
+};
+
+// Stream-K segments: CTA c owns units [seg(c), seg(c+1)) of the U units laid end to end in item
+// order. Item p costs its steps (units [start, start + steps), real key blocks) plus kPieceCost
+// trailing units for its start and end, so a CTA given many short items is given fewer steps;
+// a segment boundary inside those trailing units cuts nothing. All G heads of a row tile take the
+// tile's steps ts[t], so the layout has a closed form over tc[], the tiles' inclusive prefix of
+// (ts + kPieceCost): a KV group spans UG = G * tc[ntiles-1] units and item (g, t, hh) starts at
+// g * UG + G * tc[t-1] + hh * (ts[t] + kPieceCost).
+struct Plan {
+  const int* ts;
+  const int* tc;
+  int G, ntiles;
+  long long UG, U;
+  int grid;
+  __device__ __forceinline__ long long seg(int c) const { return (long long)c * U / grid; }
+  __device__ __forceinline__ int steps(int p) const { return ts[(p % (G * ntiles)) / G]; }
+  __device__ __forceinline__ long long start_of(int p) const {
+    const int g = p / (G * ntiles), r = p - g * G * ntiles, t = r / G, hh = r - t * G;
+    return g * UG + (long long)G * (t ? tc[t - 1] : 0) + (long long)hh * (ts[t] + kPieceCost);
+  }
+  __device__ __forceinline__ int item_at(long long u) const {  // the item whose units hold unit u
+    const int g = (int)(u / UG);
+    const long long r = u - g * UG;
+    int lo = 0, hi = ntiles - 1;  // first tile t with G * tc[t] > r
+    while (lo < hi) {
+      const int mid = (lo + hi) >> 1;
+      if ((long long)G * tc[mid] > r) hi = mid; else lo = mid + 1;
+    }
+    const int hh = (int)((r - (long long)G * (lo ? tc[lo - 1] : 0)) / (ts[lo] + kPieceCost));
+    return g * G * ntiles + lo * G + hh;
+  }
+  __device__ __forceinline__ int cta_of(long long u) const {  // the CTA whose segment holds unit u
+    int c = (int)((u * grid) / U);
+    while (c + 1 < grid && seg(c + 1) <= u) ++c;
+    while (c > 0 && seg(c) > u) --c;
+    return c;
+  }
+  // workspace slot of item p's piece in CTA cx: 2cx if it is the first real piece of cx's segment
+  // (no earlier item's real steps in it), else 2cx + 1
+  __device__ __forceinline__ int slot_of(int p, int cx) const {
+    return 2 * cx + ((p == 0 || seg(cx) >= start_of(p) - kPieceCost) ? 0 : 1);
+  }
+};
+
+__device__ __forceinline__ unsigned atom_add_acq_rel_gpu(unsigned* p, unsigned v) {
+  unsigned old;
+  asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], %2;" : "=r"(old) : "l"(p), "r"(v) : "memory");
+  return old;
+}
+
+template <typename T>
+__global__ void __launch_bounds__(kThreadsTC, 1)
+    attn_rows_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
+                        const __grid_constant__ CUtensorMap tm_v, const int64_t* __restrict__ pos, int R, int Hq,
+                        int G, long long T_cache, float scale_log2, T* __restrict__ out, unsigned* err,
+                        unsigned char* __restrict__ ws, int stream_k) {
+  extern __shared__ __align__(1024) unsigned char smem_raw[];
+  unsigned char* smem =
+      reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  unsigned char* sQ = smem;               // 2 buffers x 2 blocks (d 0-63, d 64-127)
+  unsigned char* sK = smem + 4 * kBlock;  // 2 stages x 2 blocks
+  unsigned char* sV = smem + 8 * kBlock;  // 2 stages x 2 blocks
+  int* s_tsteps = reinterpret_cast<int*>(smem + kTilesBytes);  // [tile] steps
+  int* s_tpre = s_tsteps + kMaxTiles;  // [tile] inclusive prefix of steps + kPieceCost
+  uint64_t* bars = reinterpret_cast<uint64_t*>(s_tpre + kMaxTiles);
+  uint64_t* q_full = bars + 0;   // [2] Q buffer loaded
+  uint64_t* k_full = bars + 2;   // [2] K stage loaded
+  uint64_t* v_full = bars + 4;   // [2] V stage loaded
+  uint64_t* s_full = bars + 6;   // [2] S buffer written by QK
+  uint64_t* q_free = bars + 8;   // [2] Q buffer read by its piece's last QK
+  uint64_t* o_free = bars + 10;  // O read by the piece's epilogue (256 arrivals)
+  uint64_t* p_full = bars + 11;  // [2] P of S buffer b written by the softmax (256 arrivals)
+  uint64_t* pv_done = bars + 13; // [2] PV of S buffer b's P complete (buffer reusable, O stable)
+  uint64_t* k_free = bars + 15;  // [2] K stage read by its QK
+  uint64_t* v_free = bars + 17;  // [2] V stage read by its PV
+  uint64_t* quad_bar = bars + 19; // [4] the two softmax warps of a row quadrant (64 arrivals)
+  uint64_t* soft_bar = bars + 23; // all softmax warps (256 arrivals)
+  constexpr int kNumBars = 24;
+  uint32_t* s_tmem = reinterpret_cast<uint32_t*>(bars + kNumBars);
+  int* s_abort = reinterpret_cast<int*>(bars + kNumBars + 1);
+  int* s_merge = s_abort + 1;  // [2] merge decisions of this CTA's (at most two) partial pieces
+  __shared__ float s_part[2][kWarpsPerQuad][kRows];  // [max / sum][key half][row]
+
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int ntiles = (R + kRows - 1) / kRows;
+
+  if (warp == 0) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(s_tmem)),
+                 "r"(512)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+  }
+  if (tid == 32) {
+    for (int i = 0; i < kNumBars; ++i) mbar_init(bars + i, 1);
+    mbar_init(o_free, kSoftWarps * 32);
+    mbar_init(&p_full[0], kSoftWarps * 32);
+    mbar_init(&p_full[1], kSoftWarps * 32);
+    for (int i = 0; i < 4; ++i) mbar_init(&quad_bar[i], kWarpsPerQuad * 32);
+    mbar_init(soft_bar, kSoftWarps * 32);
+    *s_abort = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+
+  // ---- steps of every row tile (one warp per tile: the latest valid position among its rows)
+  auto tile_steps = [&](int t) -> int {
+    long long mx = 0;
+#pragma unroll
+    for (int k = 0; k < kRows / 32; ++k) {
+      const int r = t * kRows + k * 32 + lane;
+      if (r < R) {
+        const long long p = pos[r];
+        if (p >= 0 && p < T_cache) mx = p > mx ? p : mx;
+      }
+    }
+#pragma unroll
+    for (int o = 16; o; o >>= 1) {
+      const long long y = __shfl_xor_sync(0xffffffffu, mx, o);
+      mx = y > mx ? y : mx;
+    }
+    return (int)(mx / kKeys) + 1;
+  };
+  if (stream_k) {
+    for (int t = warp; t < ntiles; t += kThreadsTC / 32) {
+      const int st = tile_steps(t);
+      if (lane == 0) s_tsteps[t] = st;
+    }
+    __syncthreads();
+    if (warp == 0) {  // inclusive prefix of the tiles' steps
+      int carry = 0;
+      for (int base = 0; base < ntiles; base += 32) {
+        const int t = base + lane;
+        int v = t < ntiles ? s_tsteps[t] + kPieceCost : 0;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+          const int y = __shfl_up_sync(0xffffffffu, v, o);
+          if (lane >= o) v += y;
+        }
+        if (t < ntiles) s_tpre[t] = carry + v;
+        carry += __shfl_sync(0xffffffffu, v, 31);
+      }
+    }
+  } else if (warp == 0) {
+    const int st = tile_steps(ntiles - 1 - (int)blockIdx.x / Hq);
+    if (lane == 0) s_tsteps[0] = st;
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *s_tmem;
+
+  const long long UG = stream_k ? (long long)G * s_tpre[ntiles - 1] : 0;  // units of one KV group
+  const Plan plan{s_tsteps, s_tpre, G, ntiles, UG, UG * (Hq / G), (int)gridDim.x};
+  const int c = blockIdx.x;
+  long long cur = stream_k ? plan.seg(c) : 0;
+  const long long seg_end = stream_k ? plan.seg(c + 1) : 1;
+  // this CTA's pieces, in order
+  auto first_piece = [&](Piece& pc) -> bool {
+    if (!stream_k) {  // one whole tile: latest rows first
+      pc.item = -1 - c;  // encoded below
+      pc.n_item = s_tsteps[0];
+      pc.j0 = 0;
+      pc.j1 = pc.n_item;
+      pc.first = true;
+      return true;
+    }
+    if (cur >= seg_end) return false;
+    pc.item = plan.item_at(cur);
+    long long u0 = plan.start_of(pc.item);
+    pc.n_item = plan.steps(pc.item);
+    if (cur - u0 >= pc.n_item) {  // the segment starts in an item's trailing cost units
+      u0 += pc.n_item + kPieceCost;
+      if (u0 >= seg_end) return false;
+      pc.item += 1;
+      pc.n_item = plan.steps(pc.item);
+      cur = u0;
+    }
+    pc.j0 = (int)(cur - u0);
+    pc.j1 = (int)(min(seg_end - u0, (long long)pc.n_item));
+    pc.first = true;
+    return true;
+  };
+  auto next_piece = [&](Piece& pc) -> bool {
+    if (!stream_k) return false;
+    const long long u1 = plan.start_of(pc.item) + pc.n_item + kPieceCost;  // the next item's start
+    if (u1 >= seg_end) return false;
+    pc.item += 1;
+    pc.n_item = plan.steps(pc.item);
+    pc.j0 = 0;
+    pc.j1 = (int)(min(seg_end - u1, (long long)pc.n_item));
+    pc.first = false;
+    return true;
+  };
+  auto item_coords = [&](const Piece& pc) -> Item {
+    if (pc.item < 0) {
+      const int cc = -1 - pc.item;
+      const int h = cc % Hq;
+      return Item{h, ntiles - 1 - cc / Hq, h / G};
+    }
+    return item_of(pc.item, G, ntiles);
+  };
+  const Waiter wait{s_abort};
+
+  if (warp == kLoadWarp) {
+    // ------------------------------------------------------------------ TMA loader (one lane)
+    // K and V have separate 2-stage rings; K(g+2) goes into its stage once QK(g) has read it and
+    // V(g+2) once PV(g) has, so copies run two steps ahead of the MMAs.
+    if (lane == 0) {
+      Piece pc;
+      int k = 0;
+      long long g = 0;
+      bool ok = true;
+      for (bool more = first_piece(pc); more && ok; more = next_piece(pc), ++k) {
+        const Item it = item_coords(pc);
+        const int qb = k & 1;
+        if (k >= 2 && !(ok = wait(&q_free[qb], ((k - 2) >> 1) & 1))) break;
+        mbar_expect_tx(&q_full[qb], 2 * kBlock);
+        tma_load_3d(sQ + qb * 2 * kBlock, &tm_q, &q_full[qb], 0, it.head, it.tile * kRows);
+        tma_load_3d(sQ + qb * 2 * kBlock + kBlock, &tm_q, &q_full[qb], 64, it.head, it.tile * kRows);
+        for (int j = pc.j0; j < pc.j1; ++j, ++g) {
+          const int s = (int)(g & 1);
+          const uint32_t ph = (uint32_t)(((g - 2) >> 1) & 1);
+          if (g >= 2 && !(ok = wait(&k_free[s], ph))) break;
+          mbar_expect_tx(&k_full[s], 2 * kBlock);
+          tma_load_3d(sK + s * 2 * kBlock, &tm_k, &k_full[s], 0, j * kKeys, it.kvh);
+          tma_load_3d(sK + s * 2 * kBlock + kBlock, &tm_k, &k_full[s], 64, j * kKeys, it.kvh);
+          if (g >= 2 && !(ok = wait(&v_free[s], ph))) break;
+          mbar_expect_tx(&v_full[s], 2 * kBlock);
+          tma_load_3d(sV + s * 2 * kBlock, &tm_v, &v_full[s], 0, j * kKeys, it.kvh);
+          tma_load_3d(sV + s * 2 * kBlock + kBlock, &tm_v, &v_full[s], 64, j * kKeys, it.kvh);
+        }
+      }
+    }
+  } else if (warp == kMmaWarp) {
+    // ------------------------------------------------------------------ MMA issuer (one warp)
+    constexpr uint32_t fmt = std::is_same<T, __nv_bfloat16>::value ? 1u : 0u;
+    constexpr uint32_t idesc_qk = idesc_f16(fmt, 0, kRows, kKeys);
+    constexpr uint32_t idesc_pv = idesc_f16(fmt, 1, kRows, kD);
+    // descriptors of stage 0, chunk 0; stages and chunks add (byte offset >> 4) to the address
+    const uint64_t dq = sw128_desc(smem_u32(sQ), 16, 1024), dk0 = sw128_desc(smem_u32(sK), 16, 1024);
+    const uint64_t dv0 = sw128_desc(smem_u32(sV), kBlock, 1024);
+    constexpr uint64_t kStage = (2 * kBlock) >> 4;
+    // PV(g): O_h += P_g[:, keys of half h] V_g[keys of half h, :] for h = 0, 1; P of half h sits in
+    // S buffer g%2 at columns 64*h .. 64*h+31 (packed pairs); `fresh` starts each half's O anew
+    auto issue_pv = [&](long long g, bool fresh) {
+      const int b = (int)(g & 1);
+      const uint64_t vb = dv0 + (uint64_t)b * kStage;
+#pragma unroll
+      for (int kk = 0; kk < kKeys / 16; ++kk)
+        mma_f16_ts_elect(tmem + kTmemO + (kk >> 2) * 128, tmem + b * kKeys + (kk >> 2) * 64 + (kk & 3) * 8,
+                         vb + (uint64_t)((kk * 16 * 128) >> 4), idesc_pv, (!fresh || (kk & 3) > 0) ? 1u : 0u);
+      mma_commit_elect(&pv_done[b]);
+      mma_commit_elect(&v_free[b]);
+    };
+    // Steps of all pieces in order: QK(g), then PV of the step before (possibly the previous
+    // piece's last), so the next piece's first QK goes in before the current piece's last PV and
+    // the tensor pipe does not drain at a piece boundary.
+    Piece pc;
+    int k = 0, pk = 0;
+    long long g = 0, pg = -1;  // pg: step whose PV is still to be issued
+    bool p_fresh = false, ok = true;
+    auto pv_prev = [&]() -> bool {  // PV(pg): its P, its V stage, and (a piece's first PV) O read out
+      const int b = (int)(pg & 1);
+      if (!__all_sync(0xffffffffu, wait(&p_full[b], (pg >> 1) & 1) && wait(&v_full[b], (pg >> 1) & 1) &&
+                                       (!p_fresh || pk == 0 || wait(o_free, (pk - 1) & 1))))
+        return false;
+      tc_fence_after();
+      issue_pv(pg, p_fresh);
+      return true;
+    };
+    for (bool more = first_piece(pc); more && ok; more = next_piece(pc), ++k) {
+      const int n = pc.j1 - pc.j0;
+      const int qb = k & 1;
+      const uint64_t dqk = dq + (uint64_t)qb * kStage;
+      for (int jl = 0; jl < n && ok; ++jl, ++g) {
+        const int s = (int)(g & 1);
+        // S buffer s holds P(g-2) until PV(g-2) has read it
+        ok = __all_sync(0xffffffffu, wait(&k_full[s], (g >> 1) & 1) &&
+                                         (jl > 0 || wait(&q_full[qb], (k >> 1) & 1)) &&
+                                         (g < 2 || wait(&pv_done[s], ((g - 2) >> 1) & 1)));
+        if (!ok) break;
+        tc_fence_after();
+        const uint64_t kb = dk0 + (uint64_t)s * kStage;
+#pragma unroll
+        for (int kk = 0; kk < kD / 16; ++kk) {
+          const uint64_t off = (uint64_t)(((kk >> 2) * kBlock + (kk & 3) * 32) >> 4);
+          mma_f16_elect(tmem + s * kKeys, dqk + off, kb + off, idesc_qk, kk > 0);
+        }
+        mma_commit_elect(&s_full[s]);
+        mma_commit_elect(&k_free[s]);
+        if (jl == n - 1) mma_commit_elect(&q_free[qb]);
+        if (pg >= 0 && !(ok = pv_prev())) break;
+        pg = g;
+        p_fresh = jl == 0;
+        pk = k;
+      }
+    }
+    if (ok && pg >= 0) pv_prev();
+  } else {
+    // ------------------------------------------------------------------ softmax
+    // Each key half keeps its own running max, sum and O accumulator, so the two warps of a lane
+    // quadrant never wait for each other; the halves are merged once per piece, in the epilogue.
+    const int quad = warp & 3, part = warp >> 2;
+    const int trow = quad * 32 + lane;  // row within the tile (= TMEM lane)
+    const uint32_t lane_off = (uint32_t)(quad * 32) << 16;
+    const uint32_t col = part * kColsPerWarp;
+    const uint32_t tOh = tmem + kTmemO + part * 128;  // this half's O accumulator
+    unsigned* counters = reinterpret_cast<unsigned*>(ws);
+    unsigned char* slots = ws ? ws + kCounterBytes : nullptr;
+    // bounded barriers among softmax warps (an aborting warp never strands a partner): arrive,
+    // then wait for the phase this thread's own count says is next
+    uint32_t quad_phase = 0, soft_phase = 0;
+    auto quad_sync = [&]() -> bool {
+      mbar_arrive(&quad_bar[quad]);
+      return __all_sync(0xffffffffu, wait(&quad_bar[quad], (quad_phase++) & 1));
+    };
+    auto soft_sync = [&]() -> bool {
+      mbar_arrive(soft_bar);
+      return __all_sync(0xffffffffu, wait(soft_bar, (soft_phase++) & 1));
+    };
+    Piece pc, partials[2];
+    int k = 0, npart = 0;
+    long long g = 0;
+    bool ok = true;
+    for (bool more = first_piece(pc); more && ok; more = next_piece(pc), ++k) {
+      const Item it = item_coords(pc);
+      const int row = it.tile * kRows + trow;
+      const bool live = row < R;
+      long long p = live ? pos[row] : 0;
+      if (live && (p < 0 || p >= T_cache)) {
+        if (part == 0 && err) atomicOr(err, 2u);
+        p = 0;
+      }
+      // padding rows past R (output discarded) see every key, so they never take the masking path
+      if (!live) p = (long long)pc.n_item * kKeys - 1;
+      float m = -INFINITY, l = 0.f;
+      const int n = pc.j1 - pc.j0;
+      for (int jl = 0; jl < n; ++jl, ++g) {
+        const int s = (int)(g & 1);
+        ok = __all_sync(0xffffffffu, wait(&s_full[s], (g >> 1) & 1));
+        if (!ok) break;
+        tc_fence_after();
+        float v[kColsPerWarp];
+        {
+          uint32_t r[kColsPerWarp / 32][32];
+#pragma unroll
+          for (int cc = 0; cc < kColsPerWarp / 32; ++cc)
+            tmem_ld32_async(tmem + s * kKeys + col + cc * 32 + lane_off, r[cc]);
+          asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+          for (int cc = 0; cc < kColsPerWarp / 32; ++cc)
+#pragma unroll
+            for (int i = 0; i < 32; ++i) v[cc * 32 + i] = __uint_as_float(r[cc][i]);
+        }
+        const long long key0 = (long long)(pc.j0 + jl) * kKeys + col;
+        if (__any_sync(0xffffffffu, key0 + kColsPerWarp - 1 > p)) {
+          // keys i > lim of this half are past the row's position (one 32-bit compare each)
+          const int lim = (int)max(-1LL, min((long long)kColsPerWarp, p - key0));
+#pragma unroll
+          for (int i = 0; i < kColsPerWarp; ++i)
+            if (i > lim) v[i] = -INFINITY;
+        }
+        float m4[4] = {v[0], v[1], v[2], v[3]};  // four independent 3-input max chains
+#pragma unroll
+        for (int i = 4; i < kColsPerWarp; i += 2) m4[(i >> 1) & 3] = fmax3(m4[(i >> 1) & 3], v[i], v[i + 1]);
+        const float tmax = fmax3(m4[0], m4[1], fmaxf(m4[2], m4[3]));
+        const float m_new = fmaxf(m, tmax * scale_log2);  // -inf while every key of this half is masked
+        const bool rescale = jl > 0 && m_new > m + 8.f;
+        float alpha = 1.f;
+        if (jl == 0 || rescale) {
+          alpha = m == -INFINITY ? 0.f : ex2(m - m_new);
+          l *= alpha;
+          m = m_new;
+        }
+        const float mu = m == -INFINITY ? 0.f : m;  // all-masked half: exponentials of -inf give 0
+        uint32_t pk[kColsPerWarp / 2];
+        const float2 sc2 = make_float2(scale_log2, scale_log2), nm2 = make_float2(-mu, -mu);
+        float2 l2 = make_float2(0.f, 0.f);  // even / odd key sums
+#pragma unroll
+        for (int i = 0; i < kColsPerWarp; i += 2) {
+          const float2 x = ffma2(make_float2(v[i], v[i + 1]), sc2, nm2);
+          const float2 pp = make_float2(ex2(x.x), ex2(x.y));
+          l2 = fadd2(l2, pp);
+          pk[i / 2] = pack2<T>(pp.x, pp.y);
+        }
+        l += l2.x + l2.y;
+        // this half's O must be stable (PV(g-1) complete) to rescale it; tcgen05.ld/st are
+        // warp-collective, so the warp rescales together, other lanes by 1
+        if (__any_sync(0xffffffffu, rescale)) {
+          ok = __all_sync(0xffffffffu, wait(&pv_done[s ^ 1], ((g - 1) >> 1) & 1));
+          if (!ok) break;
+          tc_fence_after();
+#pragma unroll 1
+          for (int cc = 0; cc < kD / 32; ++cc) {
+            float o[32];
+            tmem_ld32(tOh + lane_off + cc * 32, o);
+#pragma unroll
+            for (int i = 0; i < 32; ++i) o[i] *= alpha;
+            tmem_st32(tOh + lane_off + cc * 32, o);
+          }
+        }
+        // P over this warp's own S columns (already in registers): QK(g+2) waits for PV(g)
+        tmem_st32u(tmem + s * kKeys + part * 64 + lane_off, pk);
+        asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+        tc_fence_before();
+        mbar_arrive(&p_full[s]);
+      }
+      if (!ok) break;
+      // ---- epilogue of the piece: O final once its last PV completed (PV(g-2), on the other
+      // buffer, completed before QK(g-1) was issued)
+      ok = __all_sync(0xffffffffu, wait(&pv_done[(g - 1) & 1], ((g - 1) >> 1) & 1));
+      if (!ok) break;
+      tc_fence_after();
+      // merge the halves: O = O_0 2^(m_0 - M) + O_1 2^(m_1 - M), l = l_0 2^(m_0 - M) + l_1 2^(m_1 - M)
+      s_part[0][part][trow] = m;
+      s_part[1][part][trow] = l;
+      if (!(ok = quad_sync())) break;
+      const float m0 = s_part[0][0][trow], m1 = s_part[0][1][trow];
+      const float M = fmaxf(m0, m1);
+      const float a0 = m0 == -INFINITY ? 0.f : ex2(m0 - M), a1 = m1 == -INFINITY ? 0.f : ex2(m1 - M);
+      const float L = s_part[1][0][trow] * a0 + s_part[1][1][trow] * a1;
+      const bool whole = pc.j0 == 0 && pc.j1 == pc.n_item;
+      const float c0 = whole ? a0 / L : a0, c1 = whole ? a1 / L : a1;  // whole: L > 0 (key 0 visible)
+      T* orow = out + ((long long)row * Hq + it.head) * kD + col;
+      // partial slot layout, coalesced for a warp's 32 consecutive rows: O as [32 float4 columns]
+      // [128 rows] float4, then m [128], l [128]
+      unsigned char* my_slot = whole ? nullptr : slots + (size_t)(2 * c + (pc.first ? 0 : 1)) * kSlotBytes;
+      float own[kColsPerWarp];  // the piece's O of the warp's 64 columns (divided by L for a whole tile)
+#pragma unroll
+      for (int cc = 0; cc < kColsPerWarp / 32; ++cc) {
+        float o0[32], o1[32];
+        tmem_ld32(tmem + kTmemO + col + lane_off + cc * 32, o0);
+        tmem_ld32(tmem + kTmemO + 128 + col + lane_off + cc * 32, o1);
+#pragma unroll
+        for (int i = 0; i < 32; ++i) own[cc * 32 + i] = fmaf(o0[i], c0, o1[i] * c1);
+      }
+      tc_fence_before();
+      mbar_arrive(o_free);  // O read: the next piece's first PV may overwrite it
+      if (whole) {
+        if (live) {
+#pragma unroll
+          for (int i = 0; i < kColsPerWarp; i += 8) {
+            uint4 w = make_uint4(pack2<T>(own[i], own[i + 1]), pack2<T>(own[i + 2], own[i + 3]),
+                                 pack2<T>(own[i + 4], own[i + 5]), pack2<T>(own[i + 6], own[i + 7]));
+            *reinterpret_cast<uint4*>(orow + i) = w;
+          }
+        }
+        if (!(ok = quad_sync())) break;  // s_part is rewritten by the next piece's epilogue
+        continue;
+      }
+      {
+        float4* dst = reinterpret_cast<float4*>(my_slot) + (size_t)(col / 4) * kRows + trow;
+#pragma unroll
+        for (int i = 0; i < kColsPerWarp / 4; ++i)
+          __stcg(dst + (size_t)i * kRows, make_float4(own[4 * i], own[4 * i + 1], own[4 * i + 2], own[4 * i + 3]));
+      }
+      // ---- partial: (M, L) beside O; counted in (and perhaps merged) after the CTA's last piece
+      float* ml = reinterpret_cast<float*>(my_slot + (size_t)kRows * kD * 4);
+      if (part == 0) {
+        __stcg(ml + trow, M);
+        __stcg(ml + kRows + trow, L);
+      }
+      if (!(ok = quad_sync())) break;  // s_part is rewritten by the next piece's epilogue
+      if (npart < 2) partials[npart++] = pc;
+    }
+    // ---- publish this CTA's partial pieces (its first and / or last): every softmax thread's slot
+    // writes precede the barrier (CTA-scope release / acquire); one thread counts each piece in
+    // with a device-scope acquire-release atomic, and the piece that completes its item merges it
+    if (ok && npart > 0) ok = soft_sync();
+    if (ok && npart > 0 && tid == 0) {
+      for (int i = 0; i < npart; ++i) {
+        const long long u0 = plan.start_of(partials[i].item);
+        const int c_lo = plan.cta_of(u0), c_hi = plan.cta_of(u0 + partials[i].n_item - 1);
+        unsigned pieces = 0;  // one per CTA with a non-empty segment in [c_lo, c_hi]
+        for (int cx = c_lo; cx <= c_hi; ++cx) pieces += plan.seg(cx) < plan.seg(cx + 1);
+        s_merge[i] = atom_add_acq_rel_gpu(&counters[partials[i].item], 1u) + 1 == pieces;
+      }
+    }
+    if (ok && npart > 0) ok = soft_sync();
+    for (int i = 0; ok && i < npart; ++i) {
+      if (!s_merge[i]) continue;
+      const Piece& pm = partials[i];
+      const Item it = item_coords(pm);
+      const int row = it.tile * kRows + trow;
+      const long long u0 = plan.start_of(pm.item);
+      const int c_lo = plan.cta_of(u0), c_hi = plan.cta_of(u0 + pm.n_item - 1);
+      auto slot_of = [&](int cx) { return slots + (size_t)plan.slot_of(pm.item, cx) * kSlotBytes; };
+      float Mx = -INFINITY;
+      for (int cx = c_lo; cx <= c_hi; ++cx) {
+        if (plan.seg(cx) == plan.seg(cx + 1)) continue;  // empty segment: no piece
+        Mx = fmaxf(Mx, __ldcg(reinterpret_cast<const float*>(slot_of(cx) + (size_t)kRows * kD * 4) + trow));
+      }
+      float acc[kColsPerWarp], den = 0.f;
+#pragma unroll
+      for (int j = 0; j < kColsPerWarp; ++j) acc[j] = 0.f;
+      for (int cx = c_lo; cx <= c_hi; ++cx) {
+        if (plan.seg(cx) == plan.seg(cx + 1)) continue;
+        const unsigned char* sl = slot_of(cx);
+        const float* mlx = reinterpret_cast<const float*>(sl + (size_t)kRows * kD * 4);
+        const float mk = __ldcg(mlx + trow), lk = __ldcg(mlx + kRows + trow);
+        float4 x[kColsPerWarp / 4];  // all of this piece's loads in flight together
+        const float4* src = reinterpret_cast<const float4*>(sl) + (size_t)(col / 4) * kRows + trow;
+#pragma unroll
+        for (int j = 0; j < kColsPerWarp / 4; ++j) x[j] = __ldcg(src + (size_t)j * kRows);
+        const float wk = mk == -INFINITY ? 0.f : ex2(mk - Mx);
+        den += wk * lk;
+#pragma unroll
+        for (int j = 0; j < kColsPerWarp / 4; ++j) {
+          acc[4 * j] = fmaf(x[j].x, wk, acc[4 * j]);
+          acc[4 * j + 1] = fmaf(x[j].y, wk, acc[4 * j + 1]);
+          acc[4 * j + 2] = fmaf(x[j].z, wk, acc[4 * j + 2]);
+          acc[4 * j + 3] = fmaf(x[j].w, wk, acc[4 * j + 3]);
+        }
+      }
+      if (row < R) {
+        const float inv = den > 0.f ? 1.f / den : 0.f;
+        T* orow = out + ((long long)row * Hq + it.head) * kD + col;
+#pragma unroll
+        for (int j = 0; j < kColsPerWarp; j += 8) {
+          uint4 w = make_uint4(pack2<T>(acc[j] * inv, acc[j + 1] * inv), pack2<T>(acc[j + 2] * inv, acc[j + 3] * inv),
+                               pack2<T>(acc[j + 4] * inv, acc[j + 5] * inv), pack2<T>(acc[j + 6] * inv, acc[j + 7] * inv));
+          *reinterpret_cast<uint4*>(orow + j) = w;
+        }
+      }
+      if (tid == 0) counters[pm.item] = 0u;  // every piece has counted in: ready for the next call
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (*s_abort && tid == 0) {
+    if (err) atomicOr(err, 4u);
+    // let copies and MMAs already issued land before the CTA's resources go away: each barrier
+    // an async unit arrives on gets a short bounded wait on both parities
+    for (int b = 0; b < 2; ++b)
+      for (int i = 0; i < kNumBars; ++i)
+        if (i < 10 || (i >= 13 && i < 19)) mbar_wait(bars + i, b, kAbortWaitNs);
+  }
+  __syncthreads();
+  if (warp == 0) {
+    tc_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(512) : "memory");
+  }
+}
+
+int sm_count() {
+  static int cache[128] = {0};
+  int d = 0;
+  if (cudaGetDevice(&d) != cudaSuccess || d < 0 || d >= 128) return 148;
+  if (!cache[d]) {
+    int n = 0;
+    if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, d) != cudaSuccess || n <= 0) n = 148;
+    cache[d] = n;
+  }
+  return cache[d];
+}
+
 template <typename T>
 int launch_tc(const void* q, const void* K, const void* V, long long c_sh, long long T_cache, const int64_t* pos,
-              int R, int Hq, int Hkv, float sm_scale, void* out, unsigned* err, cudaStream_t st) {
+              int R, int Hq, int Hkv, float sm_scale, void* out, unsigned* err, void* ws, size_t ws_bytes,
+              bool force_stream_k, cudaStream_t st) {
   const CUtensorMapDataType dt =
       std::is_same<T, __nv_bfloat16>::value ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
   CUtensorMap mq, mk, mv;
@@ -627,26 +707,40 @@ int launch_tc(const void* q, const void* K, const void* V, long long c_sh, long 
       attr_rc = cudaFuncSetAttribute(attn_rows_tc_kernel<__half>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem);
   });
   TREAD_CHECK_CUDA(attr_rc);
+  const long long ntiles = ((long long)R + kRows - 1) / kRows;
+  const long long nitems = (long long)Hq * ntiles;
+  const int sms = sm_count();
+  // Stream-K pays a few steps per piece plus a merge per split tile; measured on B200 it wins when
+  // the tiles do not fill one wave of SMs (e.g. a request's query rows alone: 64 rows x 28 heads),
+  // and whole tiles, latest first, win from about two waves on. force_stream_k overrides (tests).
+  const bool stream_k = ws != nullptr && ws_bytes >= kCounterBytes + (size_t)2 * sms * kSlotBytes &&
+                        nitems <= kMaxItems && ntiles <= kMaxTiles && (force_stream_k || nitems <= sms);
   const float log2e = 1.4426950408889634f;
-  dim3 grid(Hq, (R + kRows - 1) / kRows);
-  attn_rows_tc_kernel<T><<<grid, kThreadsTC, kSmem, st>>>(mq, mk, mv, pos, R, Hq, Hq / Hkv, T_cache, sm_scale * log2e,
-                                                   static_cast<T*>(out), err);
+  attn_rows_tc_kernel<T><<<stream_k ? sms : (int)nitems, kThreadsTC, kSmem, st>>>(
+      mq, mk, mv, pos, R, Hq, Hq / Hkv, T_cache, sm_scale * log2e, static_cast<T*>(out), err,
+      static_cast<unsigned char*>(stream_k ? ws : nullptr), stream_k ? 1 : 0);
   TREAD_CHECK_LAUNCH("attn_rows_tc_kernel");
   return TREAD_OK;
 }
 
 }  // namespace
 
+size_t attn_tc_workspace_bytes() { return kCounterBytes + (size_t)2 * sm_count() * kSlotBytes; }
+
 // Tensor-core path for bf16/fp16 with head_dim 128; everything else runs on CUDA cores.
 int attn_rows_dispatch(const void* q, const void* K, const void* V, long long c_sh, long long T_cache,
                        const int64_t* pos, int R, int Hq, int Hkv, int D, float sm_scale, void* out, int dtype,
-                       unsigned* err, cudaStream_t st, int force_simt) {
-  const bool tc_ok = D == kD && (dtype == TREAD_BF16 || dtype == TREAD_F16) && !force_simt &&
+                       unsigned* err, void* ws, size_t ws_bytes, cudaStream_t st, int flags) {
+  const bool tc_ok = D == kD && (dtype == TREAD_BF16 || dtype == TREAD_F16) && !(flags & 1) &&
                      (reinterpret_cast<uintptr_t>(q) % 16 == 0) && (reinterpret_cast<uintptr_t>(K) % 16 == 0) &&
-                     (reinterpret_cast<uintptr_t>(V) % 16 == 0) && (c_sh * 2) % 16 == 0 && R <= 0x7fffffff - kRows;
+                     (reinterpret_cast<uintptr_t>(V) % 16 == 0) && (c_sh * 2) % 16 == 0 && R <= 0x7fffffff - kRows &&
+                     (long long)Hq * ((R + kRows - 1) / kRows) <= 0x7fffffff;
   if (!tc_ok) return attn_rows_simt(q, K, V, c_sh, T_cache, pos, R, Hq, Hkv, D, sm_scale, out, dtype, err, st);
-  if (dtype == TREAD_BF16) return launch_tc<__nv_bfloat16>(q, K, V, c_sh, T_cache, pos, R, Hq, Hkv, sm_scale, out, err, st);
-  return launch_tc<__half>(q, K, V, c_sh, T_cache, pos, R, Hq, Hkv, sm_scale, out, err, st);
+  if (dtype == TREAD_BF16)
+    return launch_tc<__nv_bfloat16>(q, K, V, c_sh, T_cache, pos, R, Hq, Hkv, sm_scale, out, err, ws, ws_bytes,
+                                    (flags & 2) != 0, st);
+  return launch_tc<__half>(q, K, V, c_sh, T_cache, pos, R, Hq, Hkv, sm_scale, out, err, ws, ws_bytes, (flags & 2) != 0,
+                           st);
 }
 
 }  // namespace tread

@@ -325,10 +325,36 @@ def rope_rows(qkv, pos, Hq, Hkv, D, q_out, K, V, inv_freq, attn_scaling=1.0, err
     return q_out
 
 
-def attn_rows(q, K, V, pos, out=None, sm_scale=None, err=None, stream=None, cuda_cores=False):
+_attn_ws = {}
+
+
+def attn_workspace(device):
+    """The zero-filled stream-K workspace of tread_attn_rows on `device` (allocated once, then kept:
+    captured CUDA graphs hold its address). Calls sharing it must be stream-ordered."""
+    idx = torch.device(device).index
+    ws = _attn_ws.get(idx)
+    if ws is None:
+        with torch.cuda.device(device):
+            n = C.lib().tread_attn_rows_workspace_bytes()
+        ws = torch.zeros(n, dtype=torch.uint8, device=device)
+        _attn_ws[idx] = ws
+    return ws
+
+
+def reset_attn_workspace(device):
+    """Zero the workspace's counters again (needed only after a kernel gave up on a wait)."""
+    ws = _attn_ws.get(torch.device(device).index)
+    if ws is not None:
+        ws.zero_()
+
+
+def attn_rows(q, K, V, pos, out=None, sm_scale=None, err=None, stream=None, cuda_cores=False, workspace=True,
+              stream_k=False):
     """Each row of q [R, Hq, D] attends to keys at positions <= pos[row] of the layer cache K/V
     ([Hkv, T, D]) with GQA (tread/blend.py:76,110). Returns out [R, Hq, D]. bf16/fp16 with D=128
-    run on tensor cores unless `cuda_cores`."""
+    run on tensor cores unless `cuda_cores`. With `workspace` (default) the tensor-core kernel may
+    use the stream-K schedule over the device's shared workspace (it does when the row tiles do not
+    fill one wave of SMs; `stream_k` forces it); without it every CTA runs one whole row tile."""
     C.require_cuda(q, "q")
     K = _layer_cache(K, "K")
     V = _layer_cache(V, "V")
@@ -342,11 +368,13 @@ def attn_rows(q, K, V, pos, out=None, sm_scale=None, err=None, stream=None, cuda
         out = torch.empty_like(q)
     if sm_scale is None:
         sm_scale = D ** -0.5
+    ws = attn_workspace(q.device) if workspace and not cuda_cores else None
+    flags = 1 if cuda_cores else (2 if stream_k else 0)
     with torch.cuda.device(q.device):
         rc = C.lib().tread_attn_rows(q.data_ptr(), K.data_ptr(), V.data_ptr(), K.stride(0), K.shape[1], pos.data_ptr(),
-                                     R, Hq, Hkv, D, float(sm_scale), out.data_ptr(), C.dtype_code(q.dtype),
-                                     1 if cuda_cores else 0, None if err is None else err.data_ptr(),
-                                     _stream_arg(stream, q.device))
+                                     R, Hq, Hkv, D, float(sm_scale), out.data_ptr(), C.dtype_code(q.dtype), flags,
+                                     None if err is None else err.data_ptr(), None if ws is None else ws.data_ptr(),
+                                     0 if ws is None else ws.numel(), _stream_arg(stream, q.device))
     C.check(rc, "tread_attn_rows")
     return out
 

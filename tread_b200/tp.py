@@ -224,4 +224,6 @@ class TPQwen2Rows(Qwen2Rows):
         if int(e.item()):
             self.err.zero_()
             sel.zero_()
+            if int(e.item()) & 4:
+                kernels.reset_attn_workspace(self.device)
             raise RuntimeError(f"tread_b200 kernel reported an error on some rank (flags {int(e):#x})")
