@@ -735,10 +735,17 @@ def run_serving_dp(args, dev, world, rank):
     plus a 64-token query; 20% recompute. Each replica's GPU block budget is 25% of its shard of
     the pool's bytes, so the LRU spills to the pinned-host tier and fetches back.
 
-    The offered load is a closed loop: every replica serves one request per round (the rounds are
-    the exchange steps), so N requests are in flight. Untimed warm-up rounds fill the stores, then
-    --dp-rounds rounds are timed: TTFT per request by wall clock (host ids in, first token out),
-    requests/s = N x rounds / the max over ranks of the timed region's length."""
+    Load: 64 closed-loop clients spread over the N replicas, each client sending its next request
+    as soon as the previous one's first token is back. A replica serves its queue one request at
+    a time (the reference server serialises GPU work, tread/server.py:186-192) and the replicas
+    step in lockstep rounds (the rounds are the block-exchange steps), one request each per round.
+    Untimed warm-up rounds fill the stores, then --dp-rounds rounds are timed. A request's TTFT is
+    its queueing time plus its service time (host ids in, first token out, wall clock); the
+    service time alone is reported too. requests/s = N x rounds / the max over ranks of the timed
+    region's length. Tier transfers are timed with CUDA events on the store's transfer stream
+    (spill / fetch GB/s); the fetch overlap is the share of fetch time the compute stream did not
+    wait for (it ran under the request's other work: lookups, cold prefills, resident blocks'
+    assembly)."""
     import torch.distributed as dist
 
     from tread_b200 import BlockStore
@@ -766,8 +773,11 @@ def run_serving_dp(args, dev, world, rank):
         idx = torch.multinomial(w, k, replacement=False, generator=rg)
         return [pool[i] for i in idx.tolist()], random_tokens(64, V, rg)
 
+    from tread_b200.engine import fetch_overlap
+
     warm = 10
-    ttft, st_all = [], []
+    clients = max(1, 64 // world)  # closed-loop clients this replica serves
+    service, done, st_all = [], [], []
     s0 = None
     for rnd in range(warm + args.dp_rounds):
         if rnd == warm:
@@ -776,6 +786,8 @@ def run_serving_dp(args, dev, world, rank):
             t_start = time.perf_counter()
             s0 = dict(vars(eng.store.stats))
             b0 = (eng.shards.sent_bytes, eng.shards.recv_bytes)
+            eng.store.timing = True
+            eng.store.transfers, eng.fetch_waits = [], []
         docs, query = request()
         t0 = time.perf_counter()
         logits, cache, st = eng.serve(prefix, docs, query, ratio=0.2)
@@ -783,32 +795,57 @@ def run_serving_dp(args, dev, world, rank):
         t1 = time.perf_counter()
         del cache
         if rnd >= warm:
-            ttft.append(t1 - t0)
+            service.append(t1 - t0)
+            done.append(t1)
             st_all.append(st)
     torch.cuda.synchronize(dev)
     elapsed = max_over_ranks(time.perf_counter() - t_start, world, dev)
+    overlap = fetch_overlap(eng.store, eng)
+    rates = eng.store.transfer_rates()
+    eng.store.timing = False
+    eng.fetch_waits = []
+    # FIFO over this replica's clients: request j was sent when request j - clients finished
+    ttft = [done[j] - (done[j - clients] if j >= clients else t_start) for j in range(len(done))]
     s1 = vars(eng.store.stats)
     d = {k: s1[k] - s0[k] for k in ("hits", "misses", "evictions", "cpu_hits", "offloads")}
     t = torch.tensor(ttft, dtype=torch.float64, device=dev)
+    sv = torch.tensor(service, dtype=torch.float64, device=dev)
     req_hits = sum(s_.hits for s_ in st_all)
     req_blocks = sum(s_.hits + s_.misses for s_ in st_all)
     peer = float(eng.shards.sent_bytes - b0[0])
+    xfer = [rates["spill"]["bytes"], rates["spill"]["ms"], rates["fetch"]["bytes"], rates["fetch"]["ms"]]
+    ov = [overlap or 0.0, 1.0 if overlap is not None else 0.0]
     if world > 1:
         parts = [torch.empty_like(t) for _ in range(world)]
         dist.all_gather(parts, t)
         t = torch.cat(parts)
-        tot = torch.tensor([d["hits"], d["misses"], d["cpu_hits"], d["offloads"], peer, req_hits, req_blocks],
+        parts = [torch.empty_like(sv) for _ in range(world)]
+        dist.all_gather(parts, sv)
+        sv = torch.cat(parts)
+        tot = torch.tensor([d["hits"], d["misses"], d["cpu_hits"], d["offloads"], peer, req_hits, req_blocks] + xfer + ov,
                            dtype=torch.float64, device=dev)
         dist.all_reduce(tot)
-        d["hits"], d["misses"], d["cpu_hits"], d["offloads"], peer, req_hits, req_blocks = tot.tolist()
+        vals = tot.tolist()
+        d["hits"], d["misses"], d["cpu_hits"], d["offloads"], peer, req_hits, req_blocks = vals[:7]
+        xfer, ov = vals[7:11], vals[11:13]
+        ov = [ov[0] / ov[1] if ov[1] else 0.0, ov[1]]
     t = t.cpu().sort().values
+    sv = sv.cpu().sort().values
+    gbs = lambda nb, ms: round(nb / (ms * 1e-3) / 1e9, 2) if ms > 0 else None
     n_req = world * args.dp_rounds
     out = {"workload": "configs[4] 7B replicas, 512-doc pool (256-2048 tokens, Zipf 1.1), 8-24 docs + 256 prefix "
                        "+ 64 query, 20% recompute, GPU budget 25% of each hash shard",
            "replicas": world, "rounds": args.dp_rounds, "warmup_rounds": warm,
+           "clients": 64, "clients_per_replica": clients,
            "requests_per_s": round(n_req / elapsed, 2),
            "ttft_p50_ms": round(float(t[len(t) // 2]) * 1e3, 2),
            "ttft_p99_ms": round(float(t[min(len(t) - 1, int(0.99 * len(t)))]) * 1e3, 2),
+           "service_p50_ms": round(float(sv[len(sv) // 2]) * 1e3, 2),
+           "service_p99_ms": round(float(sv[min(len(sv) - 1, int(0.99 * len(sv)))]) * 1e3, 2),
+           "spill_gbs": gbs(xfer[0], xfer[1]), "fetch_gbs": gbs(xfer[2], xfer[3]),
+           "spill_gb_per_request": round(xfer[0] / n_req / 1e9, 3),
+           "fetch_gb_per_request": round(xfer[2] / n_req / 1e9, 3),
+           "fetch_overlap_frac": round(ov[0], 3) if ov[1] else None,
            "store_lookups": {"hits": int(d["hits"]), "misses": int(d["misses"]), "cpu_tier_hits": int(d["cpu_hits"]),
                              "offloads": int(d["offloads"])},
            "request_block_hit_rate": round(req_hits / max(1, req_blocks), 4),

@@ -53,6 +53,19 @@ class _Tmp:
         pass
 
 
+def fetch_overlap(store, engine):
+    """Share of the logged fetch time (host tier -> HBM copies on the store's transfer stream) that
+    the compute stream did not wait for, i.e. that ran under other work of the requests: 1 minus
+    the device time of the engine's waits on still-running fetches (recorded while `store.timing`
+    is on) over the fetches' own device time. Synchronises the device."""
+    torch.cuda.synchronize()
+    fetch_ms = sum(a.elapsed_time(b) for k, a, b, _ in store.transfers if k == "fetch")
+    if fetch_ms <= 0:
+        return None
+    waited = sum(max(0.0, a.elapsed_time(b)) for a, b in engine.fetch_waits)
+    return max(0.0, 1.0 - waited / fetch_ms)
+
+
 def _split_ids(segments, device):
     """Host (CPU int64) and device views of a request's token-id segments with at most one
     device->host and one host->device copy: block keys hash host ids, kernels read device ids.
@@ -79,6 +92,7 @@ class Engine:
             # a request graph would capture the tensor-parallel all-reduces: not supported
             raise ValueError("graphs=True is not supported with tensor-parallel rows")
         self.runner = SubsetRunner(model) if graphs else None
+        self.fetch_waits = []  # (start, end) events of compute-stream waits on fetches, while the store times
         cfg = model.config
         self.sig = (cfg._name_or_path, str(model.dtype), getattr(cfg, "rope_theta", None),
                     getattr(cfg, "rope_scaling", None))
@@ -213,10 +227,19 @@ class Engine:
             cands = list(torch.arange(P, offset, device=docs[0].device).split([len(d) for d in docs]))
         ready = [s for s in segs if s[0].ready is None or s[0].ready.query()]
         pending = [s for s in segs if not (s[0].ready is None or s[0].ready.query())]
+        timing = getattr(self.store, "timing", False) and torch.cuda.is_available()
         for group in (ready, pending):
             if group:
+                if timing and group is pending:
+                    # the device time the compute stream spends waiting for still-running fetches
+                    a = torch.cuda.Event(enable_timing=True)
+                    a.record()
                 for b, _, _ in group:
                     b.wait()
+                if timing and group is pending:
+                    z = torch.cuda.Event(enable_timing=True)
+                    z.record()
+                    self.fetch_waits.append((a, z))
                 kernels.rope_gather_append([(b.K, b.V, dl, o) for b, dl, o in group], K, V, net.inv_freq,
                                            net.attn_scaling)
         self._sync()

@@ -58,13 +58,18 @@ class Block:
 
 @dataclass
 class StoreStats:
-    hits: int = 0  # GPU + CPU-tier hits
+    """Counters with the reference's field names and meanings: `hits` counts lookups served by
+    either tier (`cpu_hits` those served from pinned host memory); `evictions` counts every block
+    pushed out of HBM, whether it moved to the host tier (`offloads`) or was discarded;
+    `cpu_evictions` counts blocks discarded from the host tier; `bytes_used` / `cpu_bytes_used`
+    are the bytes each tier holds now."""
+    hits: int = 0
     misses: int = 0
-    evictions: int = 0  # blocks leaving the GPU tier (offloaded or dropped)
-    bytes_used: int = 0  # GPU tier
+    evictions: int = 0
+    bytes_used: int = 0
     cpu_hits: int = 0
     offloads: int = 0
-    cpu_evictions: int = 0  # blocks dropped for good from the CPU tier
+    cpu_evictions: int = 0
     cpu_bytes_used: int = 0
 
 
@@ -77,6 +82,10 @@ class BlockStore:
         self.stats = StoreStats()
         self._xfer = {}  # device index -> transfer stream
         self._inflight = []  # (event, tensors) kept alive until the copy reading them completes
+        # (kind, start event, end event, bytes) of every tier transfer while `timing` is on; no
+        # host synchronisation until transfer_rates() reads them
+        self.timing = False
+        self.transfers = []
 
     def transfer_stream(self, device):
         idx = torch.device(device).index or 0
@@ -110,7 +119,7 @@ class BlockStore:
     def put(self, key, K, V, base):
         nbytes = sum(t.numel() * t.element_size() for t in (K, V))
         if nbytes > self.budget:
-            return None  # never fits; serve this request without caching
+            return None  # larger than the whole HBM budget: the caller uses the K/V uncached
         for tier in (self.blocks, self.cpu_blocks):
             if key in tier:
                 self._remove(tier, key)
@@ -134,8 +143,8 @@ class BlockStore:
             _, old = self.cpu_blocks.popitem(last=False)
             self.stats.cpu_bytes_used -= old.nbytes
             self.stats.cpu_evictions += 1
-        # A new Block, never a mutated one: a request that looked this block up may still be
-        # assembling from its GPU tensors (tread/store.py:109-110).
+        # The host copy is a separate Block object: the HBM one may still be in use by a request
+        # that fetched it earlier (tread/store.py:109-110).
         self.cpu_blocks[key] = self._spill(b)
         self.stats.cpu_bytes_used += b.nbytes
         self.stats.offloads += 1
@@ -160,8 +169,10 @@ class BlockStore:
         hv = torch.empty(b.V.shape, dtype=b.V.dtype, pin_memory=True)
         b.wait()
         xs.wait_stream(torch.cuda.current_stream(b.K.device))  # producer kernels finished
+        t0 = self._mark(xs)
         kernels.kv_spill(hk, b.K, xs)
         kernels.kv_spill(hv, b.V, xs)
+        self._log("spill", t0, xs, b.nbytes)
         b.K.record_stream(xs)  # keep the HBM alive until the copy has read it
         b.V.record_stream(xs)
         ev = torch.cuda.Event()
@@ -176,14 +187,41 @@ class BlockStore:
         dk = torch.empty(b.K.shape, dtype=b.K.dtype, device=b.device)
         dv = torch.empty(b.V.shape, dtype=b.V.dtype, device=b.device)
         xs.wait_stream(torch.cuda.current_stream(b.device))  # the fresh allocations are free to write
+        t0 = self._mark(xs)
         kernels.kv_fetch(dk, b.K, xs)  # stream-ordered after this block's spill on the same stream
         kernels.kv_fetch(dv, b.V, xs)
+        self._log("fetch", t0, xs, b.nbytes)
         dk.record_stream(xs)
         dv.record_stream(xs)
         b.ready = torch.cuda.Event()
         b.ready.record(xs)
         self._inflight.append((b.ready, (b.K, b.V)))  # the pinned source must outlive the DMA
         b.K, b.V = dk, dv
+
+    def _mark(self, stream):
+        if not self.timing:
+            return None
+        ev = torch.cuda.Event(enable_timing=True)
+        ev.record(stream)
+        return ev
+
+    def _log(self, kind, t0, stream, nbytes):
+        if t0 is not None:
+            self.transfers.append((kind, t0, self._mark(stream), nbytes))
+
+    def transfer_rates(self, reset=True):
+        """Bytes, device milliseconds and GB/s of the spills and fetches logged while `timing` was
+        on (synchronises the device)."""
+        torch.cuda.synchronize()
+        out = {}
+        for kind in ("spill", "fetch"):
+            xs = [(a.elapsed_time(b), n) for k, a, b, n in self.transfers if k == kind]
+            ms, nb = sum(x[0] for x in xs), sum(x[1] for x in xs)
+            out[kind] = {"count": len(xs), "bytes": nb, "ms": round(ms, 3),
+                         "gbs": round(nb / (ms * 1e-3) / 1e9, 2) if ms > 0 else None}
+        if reset:
+            self.transfers = []
+        return out
 
     def _reap(self):
         self._inflight = [(e, t) for e, t in self._inflight if not e.query()]
