@@ -857,6 +857,22 @@ def run_serving_dp(args, dev, world, rank):
     return out
 
 
+def sm_clock_mhz(cycles=2_000_000):
+    """The SM clock right now: a spin of `cycles` SM cycles (torch.cuda._sleep) timed with CUDA
+    events on the current stream. Enqueued behind other work it samples the clock at that point of
+    the stream; _mhz() converts the sample once the events have completed."""
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record()
+    torch.cuda._sleep(cycles)
+    b.record()
+    return a, b, cycles
+
+
+def _mhz(sample):
+    a, b, cycles = sample
+    return round(cycles / (a.elapsed_time(b) * 1e3), 0)
+
+
 def attention_roofline(eng, S, T_ctx, nq, dev):
     """tread_attn_rows (tcgen05) on one layer of a 20% request: |S| recomputed rows + the query rows
     against the 8256-token cache, timed alone with CUDA events. Algorithmic FLOPs per call =
@@ -874,18 +890,33 @@ def attention_roofline(eng, S, T_ctx, nq, dev):
     for _ in range(3):
         kernels.attn_rows(q, K, Vc, pos, out=o)
     ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(20)]
+    torch.cuda.synchronize(dev)
+    # ~10 ms of GPU spin ahead of the timed calls: the host enqueues all of them before the GPU gets
+    # there, so each event pair brackets the kernel alone, not the host's launch latency
+    torch.cuda._sleep(20_000_000)
+    clk0 = sm_clock_mhz()
+    t0 = time.perf_counter()
     for a, b in ev:
         a.record()
         kernels.attn_rows(q, K, Vc, pos, out=o)
         b.record()
+    host_us = (time.perf_counter() - t0) / len(ev) * 1e6
+    clk1 = sm_clock_mhz()
     torch.cuda.synchronize(dev)
     us = statistics.median(a.elapsed_time(b) for a, b in ev) * 1e3
     flops = 4.0 * net.D * net.Hq * float((pos + 1).sum().item())
     peaks = load_peaks()
     tf = flops / (us * 1e-6) / 1e12
-    return {"kernel": "attn_rows_tc_kernel<bf16>", "rows": R, "us_per_layer": round(us, 1),
-            "gflop_per_layer": round(flops / 1e9, 2), "tflops": round(tf, 1), "peak_tflops": peaks["bf16_tflops"],
-            "frac": round(tf / peaks["bf16_tflops"], 4), "peak_source": peaks["tc_source"]}
+    # The calls run right after the request loop's seconds of GEMMs, under the 1 kW power cap: the
+    # SM clock is sampled just before and after them, and the fraction is also given against the
+    # sustained (power-capped) GEMM peak
+    out = {"kernel": "attn_rows_tc_kernel<bf16>", "rows": R, "us_per_layer": round(us, 1),
+           "host_enqueue_us_per_call": round(host_us, 1), "sm_mhz_before_after": [_mhz(clk0), _mhz(clk1)],
+           "gflop_per_layer": round(flops / 1e9, 2), "tflops": round(tf, 1), "peak_tflops": peaks["bf16_tflops"],
+           "frac": round(tf / peaks["bf16_tflops"], 4), "peak_source": peaks["tc_source"]}
+    if peaks.get("bf16_tflops_sustained"):
+        out["frac_of_sustained"] = round(tf / peaks["bf16_tflops_sustained"], 4)
+    return out
 
 
 def run_selector(args, dev, out_k, out_v, world):
@@ -931,6 +962,7 @@ def load_peaks():
             j = json.load(f)
         return {"hbm_gbs": float(j["hbm_gbs"]), "source": "measured (MEASURED_PEAKS.json hbm_gbs)",
                 "bf16_tflops": float(j["bf16_tflops"]),
+                "bf16_tflops_sustained": float(j["bf16_tflops_sustained"]) if j.get("bf16_tflops_sustained") else None,
                 "tc_source": "measured burst (MEASURED_PEAKS.json bf16_tflops)"}
     except Exception:
         return {"hbm_gbs": 6650.0, "source": "fallback 6.65 TB/s", "bf16_tflops": 1590.0,

@@ -193,19 +193,21 @@ int tread_rope_rows(const void* qkv, int64_t ld_qkv, const int64_t* pos, int R, 
  * [0, T_cache) skip their row and set bit 1 of *err_flag (may be NULL).
  * bf16 / fp16 with D == 128 run on the tcgen05 tensor-core kernel (TMA-fed, S, P and O in
  * TMEM). A bounded mbarrier wait that gives up sets bit 2 of *err_flag. flags bit 0 forces the
- * CUDA-core kernel (used for fp32 and the other head dims); bit 1 forces the stream-K schedule
- * below whatever the tile count (otherwise it runs only when the 128-row tiles of all heads do not
- * fill one wave of SMs).
+ * CUDA-core kernel (used for fp32 and the other head dims); bit 1 selects the stream-K schedule and
+ * bit 2 the tail-split schedule explicitly (bits 1 and 2 together are rejected).
  *
  * workspace (device, 256-byte aligned, tread_attn_rows_workspace_bytes() of it, zero-filled once by
- * the caller; may be NULL): with it, the tensor-core kernel can run one CTA per SM over equal
- * shares of all key blocks of all row tiles (stream-K), a tile split between CTAs being merged
- * from partial results kept there; the kernel returns its counters to zero, except after an error
- * of bit 2, when the caller must zero the workspace again. Without it each CTA runs one whole
- * 128-row tile. Calls that share a workspace must be stream-ordered.
+ * the caller; may be NULL): with it, the tensor-core kernel runs one CTA per SM over whole 128-row
+ * tiles, longest first, and splits the tiles left after the last full round into key ranges over
+ * the CTAs (tail split; stream-K instead gives every CTA an equal share of all tiles' key blocks).
+ * Tiles split between CTAs are merged from partial results kept in the workspace; the kernel
+ * returns its counters to zero, except after an error of bit 2, when the caller must zero the
+ * workspace again. Without it each CTA runs one whole tile. Calls that share a workspace must be
+ * stream-ordered.
  */
 #define TREAD_ATTN_FORCE_CUDA_CORES 1
 #define TREAD_ATTN_FORCE_STREAM_K 2
+#define TREAD_ATTN_FORCE_TAIL_SPLIT 4
 size_t tread_attn_rows_workspace_bytes(void);
 int tread_attn_rows(const void* q, const void* K_cache, const void* V_cache, int64_t cache_stride_head,
                     int64_t T_cache, const int64_t* q_pos, int R, int Hq, int Hkv, int D, float sm_scale,

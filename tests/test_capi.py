@@ -171,7 +171,7 @@ def _attn_call(**over):
 
 @pytest.mark.parametrize("over,needle", [
     (dict(R=-1), "R < 0"), (dict(Hq=3), "heads"), (dict(Hq=34, Hkv=2), "heads"), (dict(D=96), "head_dim"),
-    (dict(csh=10), "cache geometry"), (dict(dtype=9), "dtype"), (dict(flags=4), "flags"), (dict(out=None), "null"),
+    (dict(csh=10), "cache geometry"), (dict(dtype=9), "dtype"), (dict(flags=8), "flags"), (dict(flags=6), "flags"), (dict(out=None), "null"),
     (dict(ws=264, ws_bytes=1 << 20), "workspace"),
 ])
 def test_attn_rows_rejects_bad_arguments(over, needle):

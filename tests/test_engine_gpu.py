@@ -307,7 +307,8 @@ def _sdpa_ref(q, K, V, pos):
 
 # variants of the tensor-core kernel: the default choice, the stream-K schedule forced, one whole
 # row tile per CTA (no workspace)
-VARIANTS = {"default": {}, "stream_k": dict(stream_k=True), "whole_tiles": dict(workspace=False)}
+VARIANTS = {"default": {}, "stream_k": dict(schedule="stream_k"), "tail_split": dict(schedule="tail_split"),
+            "whole_tiles": dict(workspace=False)}
 
 
 def _check_attention(cuda, dtype, q, K, V, pos, variants=VARIANTS):

@@ -160,7 +160,7 @@ extern "C" int tread_attn_rows(const void* q, const void* K_cache, const void* V
   TREAD_CHECK_ARG(T_cache > 0 && cache_stride_head >= T_cache * D, "attn_rows: bad cache geometry");
   TREAD_CHECK_ARG(R <= 2147483647 && Hkv <= 65535, "attn_rows: grid too large");
   TREAD_CHECK_ARG(dtype_size(dtype) != 0, "attn_rows: unknown dtype %d", dtype);
-  TREAD_CHECK_ARG((flags & ~3) == 0, "attn_rows: unknown flags %#x", flags);
+  TREAD_CHECK_ARG((flags & ~7) == 0 && (flags & 6) != 6, "attn_rows: unknown flags %#x", flags);
   TREAD_CHECK_ARG(workspace == nullptr || (reinterpret_cast<uintptr_t>(workspace) & 255u) == 0,
                   "attn_rows: workspace not 256-byte aligned");
   return attn_rows_dispatch(q, K_cache, V_cache, cache_stride_head, T_cache, q_pos, R, Hq, Hkv, D, sm_scale, out,

@@ -40,6 +40,7 @@
 // must then be zeroed before the next call).
 #include <cuda.h>
 
+#include <algorithm>
 #include <mutex>
 #include <type_traits>
 
@@ -97,6 +98,15 @@ constexpr int kTilesBytes = 12 * kBlock;
 constexpr int kSmem = 1024 + kTilesBytes + 8 * kMaxTiles + 512;
 // Stream-K cost of an item's start and end (pipeline fill and drain, epilogue), in steps.
 constexpr int kPieceCost = 3;
+// Exponentials per 16 keys of a softmax lane that run as a polynomial on the FMA pipe instead of
+// the MUFU (in pairs): the MUFU's 16 ex2 per clock per SM would otherwise take as long per step as
+// the two 128-cube MMAs.
+#ifndef TREAD_ATTN_POLY_PAIRS
+#define TREAD_ATTN_POLY_PAIRS 2
+#endif
+constexpr int kPolyPairs = TREAD_ATTN_POLY_PAIRS;
+constexpr int kTailSplit = 8;  // most key ranges one tail-round tile is split into
+constexpr int kMergeCost = 3;  // units charged to a split part for its partial store and merge
 // TMEM columns: S buffers 0-127 and 128-255 (fp32; each column half also holds that half's P,
 // 16-bit pairs, once read), O accumulators of key halves 0 and 1 at 256-383 and 384-511.
 constexpr uint32_t kTmemO = 256;
@@ -126,9 +136,14 @@ __device__ __forceinline__ Item item_of(int p, int G, int ntiles) {
   return Item{g * G + (r - t * G), t, g};
 }
 
+// Schedules: kWhole, one CTA per tile, latest rows first; kStreamK, equal shares of all tiles' key
+// blocks per CTA; kTail, persistent CTAs running whole tiles latest first, the tiles left after the
+// full rounds split into key ranges over the CTAs.
+enum { kWhole = 0, kStreamK = 1, kTail = 2 };
+
 struct Piece {
   int item, j0, j1, n_item;
-  bool first;  // first piece of this CTA's segment (workspace slot 2c, else 2c+1)
+  bool first;  // stream-K: first piece of this CTA's segment (workspace slot 2c, else 2c+1)
 };
 
 // Stream-K segments: CTA c owns units [seg(c), seg(c+1)) of the U units laid end to end in item
@@ -185,7 +200,7 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
     attn_rows_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
                         const __grid_constant__ CUtensorMap tm_v, const int64_t* __restrict__ pos, int R, int Hq,
                         int G, long long T_cache, float scale_log2, T* __restrict__ out, unsigned* err,
-                        unsigned char* __restrict__ ws, int stream_k) {
+                        unsigned char* __restrict__ ws, int mode) {
   extern __shared__ __align__(1024) unsigned char smem_raw[];
   unsigned char* smem =
       reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -211,6 +226,7 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
   uint32_t* s_tmem = reinterpret_cast<uint32_t*>(bars + kNumBars);
   int* s_abort = reinterpret_cast<int*>(bars + kNumBars + 1);
   int* s_merge = s_abort + 1;  // [2] merge decisions of this CTA's (at most two) partial pieces
+  int* s_fin = s_abort + 4;    // [4] kTail: latest estimated CTA finish under split caps 1, 2, 4, 8
   __shared__ float s_part[2][kWarpsPerQuad][kRows];  // [max / sum][key half][row]
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -230,6 +246,7 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
     for (int i = 0; i < 4; ++i) mbar_init(&quad_bar[i], kWarpsPerQuad * 32);
     mbar_init(soft_bar, kSoftWarps * 32);
     *s_abort = 0;
+    for (int i = 0; i < 4; ++i) s_fin[i] = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
 
@@ -251,13 +268,14 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
     }
     return (int)(mx / kKeys) + 1;
   };
-  if (stream_k) {
+  const bool stream_k = mode == kStreamK;
+  if (mode != kWhole) {
     for (int t = warp; t < ntiles; t += kThreadsTC / 32) {
       const int st = tile_steps(t);
       if (lane == 0) s_tsteps[t] = st;
     }
     __syncthreads();
-    if (warp == 0) {  // inclusive prefix of the tiles' steps
+    if (stream_k && warp == 0) {  // inclusive prefix of the tiles' steps
       int carry = 0;
       for (int base = 0; base < ntiles; base += 32) {
         const int t = base + lane;
@@ -285,16 +303,99 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
   const int c = blockIdx.x;
   long long cur = stream_k ? plan.seg(c) : 0;
   const long long seg_end = stream_k ? plan.seg(c + 1) : 1;
+  // kWhole / kTail items are encoded -1 - i, i the position in the latest-first list (head i % Hq,
+  // row tile ntiles - 1 - i / Hq), so items run longest first. kTail: S CTAs take F full rounds in
+  // snake order (round k gives item k*S + c, or k*S + S-1 - c for odd k, pairing long with short).
+  // The r items left are split over the S CTAs by their rank in the tail round (c for even F,
+  // S-1 - c for odd): item F*S + q gets w_q = S/r key ranges, one more for the S % r longest items
+  // (q < S % r), at most a cap W; part p (of n steps) is steps [p*n/w_q, (p+1)*n/w_q) on rank
+  // first(q) + p, first(q) = q*w + min(q, S % r). Empty parts are skipped. W is the one of 1, 2, 4,
+  // 8 (kTailSplit) whose estimated latest CTA finish (full-round units + the CTA's tail part, a split
+  // part also paying kMergeCost) is lowest; W = 1 runs the tail items whole on the lightest CTAs.
+  const int nitems = Hq * ntiles;
+  const int tS = (int)gridDim.x, tF = nitems / tS, tR = nitems - tF * tS;
+  auto split_of = [&](int W, int& w, int& x) {  // parts per tail item under cap W: w, +1 for q < x
+    w = tS / tR;
+    x = tS - w * tR;
+    if (w >= W) w = W, x = 0;
+  };
+  int tW = 1, tX = 0;
+  if (mode == kTail && tR > 0) {
+    int cap = kTailSplit;
+    if (tF > 0) {  // every thread estimates some CTAs' finish under each cap; the block takes the max
+      for (int cx = tid; cx < tS; cx += kThreadsTC) {
+        int L = 0;
+        for (int k = 0; k < tF; ++k)
+          L += s_tsteps[ntiles - 1 - (k * tS + ((k & 1) ? tS - 1 - cx : cx)) / Hq] + kPieceCost;
+        const int rk = (tF & 1) ? tS - 1 - cx : cx;
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          int w, x;
+          split_of(1 << e, w, x);
+          const int hi = x * (w + 1), q = rk < hi ? rk / (w + 1) : x + (rk - hi) / w;
+          int fin = L;
+          if (q < tR) {
+            const int wq = w + (q < x ? 1 : 0), p = rk - (q * w + min(q, x));
+            const int n = s_tsteps[ntiles - 1 - (tF * tS + q) / Hq];
+            const int part = (p + 1) * n / wq - p * n / wq;
+            if (part > 0) fin += part + kPieceCost + (part < n ? kMergeCost : 0);
+          }
+          atomicMax(&s_fin[e], fin);
+        }
+      }
+      __syncthreads();
+      cap = 1;
+      for (int e = 1; e < 4; ++e)
+        if (s_fin[e] < s_fin[__ffs(cap) - 1]) cap = 1 << e;
+    }
+    split_of(cap, tW, tX);
+  }
+  auto part_first = [&](int q) { return q * tW + min(q, tX); };
+  auto nparts = [&](int q) { return tW + (q < tX ? 1 : 0); };
+  const int trank = (tF & 1) ? tS - 1 - c : c;  // this CTA's rank in the tail round
+  int tk = 0;  // kTail: index of this CTA's current piece
+  auto tail_piece = [&](Piece& pc) -> bool {
+    while (true) {
+      int i, p = 0, w = 1;
+      if (tk < tF) {
+        i = tk * tS + ((tk & 1) ? tS - 1 - c : c);
+      } else if (tk == tF) {
+        const int hi = tX * (tW + 1);
+        const int q = trank < hi ? trank / (tW + 1) : tX + (trank - hi) / tW;
+        if (q >= tR) return false;
+        p = trank - part_first(q);
+        w = nparts(q);
+        i = tF * tS + q;
+      } else {
+        return false;
+      }
+      ++tk;
+      const int n = s_tsteps[ntiles - 1 - i / Hq];
+      int j0 = 0, j1 = n;
+      if (i >= tF * tS) {
+        j0 = p * n / w;
+        j1 = (p + 1) * n / w;
+        if (j0 == j1) continue;  // fewer steps than parts
+      }
+      pc.item = -1 - i;
+      pc.n_item = n;
+      pc.j0 = j0;
+      pc.j1 = j1;
+      pc.first = false;
+      return true;
+    }
+  };
   // this CTA's pieces, in order
   auto first_piece = [&](Piece& pc) -> bool {
-    if (!stream_k) {  // one whole tile: latest rows first
-      pc.item = -1 - c;  // encoded below
+    if (mode == kWhole) {  // one whole tile: latest rows first
+      pc.item = -1 - c;
       pc.n_item = s_tsteps[0];
       pc.j0 = 0;
       pc.j1 = pc.n_item;
       pc.first = true;
       return true;
     }
+    if (mode == kTail) return tail_piece(pc);
     if (cur >= seg_end) return false;
     pc.item = plan.item_at(cur);
     long long u0 = plan.start_of(pc.item);
@@ -312,6 +413,7 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
     return true;
   };
   auto next_piece = [&](Piece& pc) -> bool {
+    if (mode == kTail) return tail_piece(pc);
     if (!stream_k) return false;
     const long long u1 = plan.start_of(pc.item) + pc.n_item + kPieceCost;  // the next item's start
     if (u1 >= seg_end) return false;
@@ -510,7 +612,8 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
 #pragma unroll
         for (int i = 0; i < kColsPerWarp; i += 2) {
           const float2 x = ffma2(make_float2(v[i], v[i + 1]), sc2, nm2);
-          const float2 pp = make_float2(ex2(x.x), ex2(x.y));
+          // kPolyPairs of every 8 pairs on the FMA pipe, the rest on the MUFU
+          const float2 pp = (i % 16) < 2 * kPolyPairs ? exp2_poly2(x) : make_float2(ex2(x.x), ex2(x.y));
           l2 = fadd2(l2, pp);
           pk[i / 2] = pack2<T>(pp.x, pp.y);
         }
@@ -555,7 +658,9 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
       T* orow = out + ((long long)row * Hq + it.head) * kD + col;
       // partial slot layout, coalesced for a warp's 32 consecutive rows: O as [32 float4 columns]
       // [128 rows] float4, then m [128], l [128]
-      unsigned char* my_slot = whole ? nullptr : slots + (size_t)(2 * c + (pc.first ? 0 : 1)) * kSlotBytes;
+      // kTail: a CTA's only partial is its last piece, in slot 2 * rank + 1
+      const int my_si = stream_k ? 2 * c + (pc.first ? 0 : 1) : 2 * trank + 1;
+      unsigned char* my_slot = whole ? nullptr : slots + (size_t)my_si * kSlotBytes;
       float own[kColsPerWarp];  // the piece's O of the warp's 64 columns (divided by L for a whole tile)
 #pragma unroll
       for (int cc = 0; cc < kColsPerWarp / 32; ++cc) {
@@ -600,11 +705,17 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
     if (ok && npart > 0) ok = soft_sync();
     if (ok && npart > 0 && tid == 0) {
       for (int i = 0; i < npart; ++i) {
-        const long long u0 = plan.start_of(partials[i].item);
-        const int c_lo = plan.cta_of(u0), c_hi = plan.cta_of(u0 + partials[i].n_item - 1);
-        unsigned pieces = 0;  // one per CTA with a non-empty segment in [c_lo, c_hi]
-        for (int cx = c_lo; cx <= c_hi; ++cx) pieces += plan.seg(cx) < plan.seg(cx + 1);
-        s_merge[i] = atom_add_acq_rel_gpu(&counters[partials[i].item], 1u) + 1 == pieces;
+        unsigned pieces = 0, cnt = 0;  // kTail: the non-empty parts of tail item q count at q
+        if (stream_k) {
+          const long long u0 = plan.start_of(partials[i].item);
+          const int c_lo = plan.cta_of(u0), c_hi = plan.cta_of(u0 + partials[i].n_item - 1);
+          for (int cx = c_lo; cx <= c_hi; ++cx) pieces += plan.seg(cx) < plan.seg(cx + 1);  // non-empty segments
+          cnt = partials[i].item;
+        } else {
+          cnt = (-1 - partials[i].item) - tF * tS;
+          pieces = (unsigned)min(partials[i].n_item, nparts((int)cnt));
+        }
+        s_merge[i] = atom_add_acq_rel_gpu(&counters[cnt], 1u) + 1 == pieces;
       }
     }
     if (ok && npart > 0) ok = soft_sync();
@@ -613,20 +724,43 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
       const Piece& pm = partials[i];
       const Item it = item_coords(pm);
       const int row = it.tile * kRows + trow;
-      const long long u0 = plan.start_of(pm.item);
-      const int c_lo = plan.cta_of(u0), c_hi = plan.cta_of(u0 + pm.n_item - 1);
-      auto slot_of = [&](int cx) { return slots + (size_t)plan.slot_of(pm.item, cx) * kSlotBytes; };
+      // the item's pieces: stream-K, one per CTA with a non-empty segment in [c_lo, c_hi]; kTail,
+      // the non-empty parts p of tail item q, on ranks first(q) + p (slot 2 * rank + 1 each)
+      int c_lo = 0, c_hi = 0, q = 0;
+      if (stream_k) {
+        const long long u0 = plan.start_of(pm.item);
+        c_lo = plan.cta_of(u0);
+        c_hi = plan.cta_of(u0 + pm.n_item - 1);
+      } else {
+        q = (-1 - pm.item) - tF * tS;
+        c_hi = nparts(q) - 1;
+      }
+      auto slot_at = [&](int cx) -> const unsigned char* {  // null: no piece there
+        if (!stream_k) {
+          const int n = pm.n_item, w = c_hi + 1;
+          if (cx * n / w == (cx + 1) * n / w) return nullptr;
+          return slots + (size_t)(2 * (part_first(q) + cx) + 1) * kSlotBytes;
+        }
+        if (plan.seg(cx) == plan.seg(cx + 1)) return nullptr;
+        return slots + (size_t)plan.slot_of(pm.item, cx) * kSlotBytes;
+      };
       float Mx = -INFINITY;
-      for (int cx = c_lo; cx <= c_hi; ++cx) {
-        if (plan.seg(cx) == plan.seg(cx + 1)) continue;  // empty segment: no piece
-        Mx = fmaxf(Mx, __ldcg(reinterpret_cast<const float*>(slot_of(cx) + (size_t)kRows * kD * 4) + trow));
+      for (int base = c_lo; base <= c_hi; base += 8) {  // 8 slots' maxima in flight together
+        float mv[8];
+#pragma unroll
+        for (int u = 0; u < 8; ++u) {
+          const unsigned char* sl = base + u <= c_hi ? slot_at(base + u) : nullptr;
+          mv[u] = sl ? __ldcg(reinterpret_cast<const float*>(sl + (size_t)kRows * kD * 4) + trow) : -INFINITY;
+        }
+#pragma unroll
+        for (int u = 0; u < 8; ++u) Mx = fmaxf(Mx, mv[u]);
       }
       float acc[kColsPerWarp], den = 0.f;
 #pragma unroll
       for (int j = 0; j < kColsPerWarp; ++j) acc[j] = 0.f;
       for (int cx = c_lo; cx <= c_hi; ++cx) {
-        if (plan.seg(cx) == plan.seg(cx + 1)) continue;
-        const unsigned char* sl = slot_of(cx);
+        const unsigned char* sl = slot_at(cx);
+        if (!sl) continue;
         const float* mlx = reinterpret_cast<const float*>(sl + (size_t)kRows * kD * 4);
         const float mk = __ldcg(mlx + trow), lk = __ldcg(mlx + kRows + trow);
         float4 x[kColsPerWarp / 4];  // all of this piece's loads in flight together
@@ -653,7 +787,7 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
           *reinterpret_cast<uint4*>(orow + j) = w;
         }
       }
-      if (tid == 0) counters[pm.item] = 0u;  // every piece has counted in: ready for the next call
+      if (tid == 0) counters[stream_k ? pm.item : q] = 0u;  // every piece has counted in: ready for the next call
     }
   }
   tc_fence_before();
@@ -688,7 +822,7 @@ int sm_count() {
 template <typename T>
 int launch_tc(const void* q, const void* K, const void* V, long long c_sh, long long T_cache, const int64_t* pos,
               int R, int Hq, int Hkv, float sm_scale, void* out, unsigned* err, void* ws, size_t ws_bytes,
-              bool force_stream_k, cudaStream_t st) {
+              int force, cudaStream_t st) {
   const CUtensorMapDataType dt =
       std::is_same<T, __nv_bfloat16>::value ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
   CUtensorMap mq, mk, mv;
@@ -710,15 +844,17 @@ int launch_tc(const void* q, const void* K, const void* V, long long c_sh, long 
   const long long ntiles = ((long long)R + kRows - 1) / kRows;
   const long long nitems = (long long)Hq * ntiles;
   const int sms = sm_count();
-  // Stream-K pays a few steps per piece plus a merge per split tile; measured on B200 it wins when
-  // the tiles do not fill one wave of SMs (e.g. a request's query rows alone: 64 rows x 28 heads),
-  // and whole tiles, latest first, win from about two waves on. force_stream_k overrides (tests).
-  const bool stream_k = ws != nullptr && ws_bytes >= kCounterBytes + (size_t)2 * sms * kSlotBytes &&
-                        nitems <= kMaxItems && ntiles <= kMaxTiles && (force_stream_k || nitems <= sms);
+  // Schedule (measured on B200): with a workspace, persistent CTAs (one per SM) over whole tiles,
+  // longest first, the tiles left after the full rounds split into key ranges (kTail); it beats
+  // both one CTA per tile and stream-K from 64 rows to 8000. Without a workspace, one CTA per whole
+  // tile. force (kStreamK / kTail, from the caller's flags) overrides the choice.
+  const bool ws_ok = ws != nullptr && ws_bytes >= kCounterBytes + (size_t)2 * sms * kSlotBytes &&
+                     nitems <= kMaxItems && ntiles <= kMaxTiles && T_cache <= (1LL << 24);
+  const int mode = !ws_ok ? kWhole : force ? force : kTail;
   const float log2e = 1.4426950408889634f;
-  attn_rows_tc_kernel<T><<<stream_k ? sms : (int)nitems, kThreadsTC, kSmem, st>>>(
+  attn_rows_tc_kernel<T><<<mode == kWhole ? (int)nitems : sms, kThreadsTC, kSmem, st>>>(
       mq, mk, mv, pos, R, Hq, Hq / Hkv, T_cache, sm_scale * log2e, static_cast<T*>(out), err,
-      static_cast<unsigned char*>(stream_k ? ws : nullptr), stream_k ? 1 : 0);
+      static_cast<unsigned char*>(mode == kWhole ? nullptr : ws), mode);
   TREAD_CHECK_LAUNCH("attn_rows_tc_kernel");
   return TREAD_OK;
 }
@@ -736,11 +872,11 @@ int attn_rows_dispatch(const void* q, const void* K, const void* V, long long c_
                      (reinterpret_cast<uintptr_t>(V) % 16 == 0) && (c_sh * 2) % 16 == 0 && R <= 0x7fffffff - kRows &&
                      (long long)Hq * ((R + kRows - 1) / kRows) <= 0x7fffffff;
   if (!tc_ok) return attn_rows_simt(q, K, V, c_sh, T_cache, pos, R, Hq, Hkv, D, sm_scale, out, dtype, err, st);
+  const int force = (flags & 2) ? kStreamK : (flags & 4) ? kTail : 0;
   if (dtype == TREAD_BF16)
-    return launch_tc<__nv_bfloat16>(q, K, V, c_sh, T_cache, pos, R, Hq, Hkv, sm_scale, out, err, ws, ws_bytes,
-                                    (flags & 2) != 0, st);
-  return launch_tc<__half>(q, K, V, c_sh, T_cache, pos, R, Hq, Hkv, sm_scale, out, err, ws, ws_bytes, (flags & 2) != 0,
-                           st);
+    return launch_tc<__nv_bfloat16>(q, K, V, c_sh, T_cache, pos, R, Hq, Hkv, sm_scale, out, err, ws, ws_bytes, force,
+                                    st);
+  return launch_tc<__half>(q, K, V, c_sh, T_cache, pos, R, Hq, Hkv, sm_scale, out, err, ws, ws_bytes, force, st);
 }
 
 }  // namespace tread

@@ -257,6 +257,27 @@ __device__ __forceinline__ float2 fadd2(float2 a, float2 b) {
   return d;
 }
 
+// 2^x for x <= 0 of two lanes on the FMA and integer pipes, leaving the MUFU free (the softmax
+// runs a share of its exponentials here). Cody-Waite style split: n = round(x) by adding 1.5 * 2^23
+// (n lands in the low mantissa bits of t), f = x - n in [-0.5, 0.5], 2^f by a cubic fitted here as
+// the minimax relative-error polynomial with p(0) = 1 (linear program over 4001 points; max relative
+// error 1.02e-4 in fp32 Horner arithmetic, below a bf16 half-ulp), and 2^n added into the exponent
+// field (t's bits shifted by 23: the mantissa's n moves into the exponent, the rest shifts out).
+// x is clamped at -126 so the exponent field stays non-negative (2^-126 is 0 after bf16 rounding).
+__device__ __forceinline__ float2 exp2_poly2(float2 x) {
+  constexpr float kRound = 12582912.f;  // 1.5 * 2^23
+  x.x = fmaxf(x.x, -126.f);
+  x.y = fmaxf(x.y, -126.f);
+  const float2 t = fadd2(x, make_float2(kRound, kRound));
+  const float2 n = fadd2(t, make_float2(-kRound, -kRound));
+  const float2 f = ffma2(n, make_float2(-1.f, -1.f), x);
+  float2 p = ffma2(f, make_float2(0.055008937f, 0.055008937f), make_float2(0.24221095f, 0.24221095f));
+  p = ffma2(p, f, make_float2(0.6932829f, 0.6932829f));
+  p = ffma2(p, f, make_float2(1.f, 1.f));
+  return make_float2(__int_as_float(__float_as_int(p.x) + (__float_as_int(t.x) << 23)),
+                     __int_as_float(__float_as_int(p.y) + (__float_as_int(t.y) << 23)));
+}
+
 __device__ __forceinline__ float fmax3(float a, float b, float c) {
   float d;
   asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));

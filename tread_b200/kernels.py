@@ -348,13 +348,17 @@ def reset_attn_workspace(device):
         ws.zero_()
 
 
+_SCHEDULES = {None: 0, "stream_k": 2, "tail_split": 4}
+
+
 def attn_rows(q, K, V, pos, out=None, sm_scale=None, err=None, stream=None, cuda_cores=False, workspace=True,
-              stream_k=False):
+              schedule=None):
     """Each row of q [R, Hq, D] attends to keys at positions <= pos[row] of the layer cache K/V
     ([Hkv, T, D]) with GQA (tread/blend.py:76,110). Returns out [R, Hq, D]. bf16/fp16 with D=128
-    run on tensor cores unless `cuda_cores`. With `workspace` (default) the tensor-core kernel may
-    use the stream-K schedule over the device's shared workspace (it does when the row tiles do not
-    fill one wave of SMs; `stream_k` forces it); without it every CTA runs one whole row tile."""
+    run on tensor cores unless `cuda_cores`. With `workspace` (default) the tensor-core kernel runs
+    one CTA per SM over the device's shared workspace: whole row tiles, longest first, with the
+    tiles left after the last full round split into key ranges; `schedule` ("tail_split" or
+    "stream_k") selects one explicitly. Without it every CTA runs one whole row tile."""
     C.require_cuda(q, "q")
     K = _layer_cache(K, "K")
     V = _layer_cache(V, "V")
@@ -369,7 +373,9 @@ def attn_rows(q, K, V, pos, out=None, sm_scale=None, err=None, stream=None, cuda
     if sm_scale is None:
         sm_scale = D ** -0.5
     ws = attn_workspace(q.device) if workspace and not cuda_cores else None
-    flags = 1 if cuda_cores else (2 if stream_k else 0)
+    if schedule not in _SCHEDULES:
+        raise ValueError(f"schedule must be one of {list(_SCHEDULES)}")
+    flags = 1 if cuda_cores else _SCHEDULES[schedule]
     with torch.cuda.device(q.device):
         rc = C.lib().tread_attn_rows(q.data_ptr(), K.data_ptr(), V.data_ptr(), K.stride(0), K.shape[1], pos.data_ptr(),
                                      R, Hq, Hkv, D, float(sm_scale), out.data_ptr(), C.dtype_code(q.dtype), flags,
