@@ -222,7 +222,8 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
   uint64_t* v_free = bars + 17;  // [2] V stage read by its PV
   uint64_t* quad_bar = bars + 19; // [4] the two softmax warps of a row quadrant (64 arrivals)
   uint64_t* soft_bar = bars + 23; // all softmax warps (256 arrivals)
-  constexpr int kNumBars = 24;
+  uint64_t* bulk_bar = bars + 24; // merge: partial slots copied into shared memory
+  constexpr int kNumBars = 25;
   uint32_t* s_tmem = reinterpret_cast<uint32_t*>(bars + kNumBars);
   int* s_abort = reinterpret_cast<int*>(bars + kNumBars + 1);
   int* s_merge = s_abort + 1;  // [2] merge decisions of this CTA's (at most two) partial pieces
@@ -250,7 +251,7 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
 
-  // ---- steps of every row tile (one warp per tile: the latest valid position among its rows)
+  // ---- steps of a row tile (one warp: the latest valid position among its rows)
   auto tile_steps = [&](int t) -> int {
     long long mx = 0;
 #pragma unroll
@@ -270,9 +271,33 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
   };
   const bool stream_k = mode == kStreamK;
   if (mode != kWhole) {
-    for (int t = warp; t < ntiles; t += kThreadsTC / 32) {
-      const int st = tile_steps(t);
-      if (lane == 0) s_tsteps[t] = st;
+    // all tiles, one warp each (tiles warp, warp + 10, ...), eight tiles' position loads in flight
+    // together before their reductions
+    constexpr int kWarps = kThreadsTC / 32;
+    for (int t0 = warp; t0 < ntiles; t0 += 8 * kWarps) {
+      long long p[8][kRows / 32];
+#pragma unroll
+      for (int k = 0; k < 8; ++k)
+#pragma unroll
+        for (int j = 0; j < kRows / 32; ++j) {
+          const int r = (t0 + k * kWarps) * kRows + j * 32 + lane;
+          p[k][j] = t0 + k * kWarps < ntiles && r < R ? pos[r] : -1;
+        }
+#pragma unroll
+      for (int k = 0; k < 8; ++k) {
+        const int t = t0 + k * kWarps;
+        if (t >= ntiles) break;  // warp-uniform
+        long long mx = 0;
+#pragma unroll
+        for (int j = 0; j < kRows / 32; ++j)
+          if (p[k][j] >= 0 && p[k][j] < T_cache) mx = p[k][j] > mx ? p[k][j] : mx;
+#pragma unroll
+        for (int o = 16; o; o >>= 1) {
+          const long long y = __shfl_xor_sync(0xffffffffu, mx, o);
+          mx = y > mx ? y : mx;
+        }
+        if (lane == 0) s_tsteps[t] = (int)(mx / kKeys) + 1;
+      }
     }
     __syncthreads();
     if (stream_k && warp == 0) {  // inclusive prefix of the tiles' steps
@@ -312,6 +337,7 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
   // first(q) + p, first(q) = q*w + min(q, S % r). Empty parts are skipped. W is the one of 1, 2, 4,
   // 8 (kTailSplit) whose estimated latest CTA finish (full-round units + the CTA's tail part, a split
   // part also paying kMergeCost) is lowest; W = 1 runs the tail items whole on the lightest CTAs.
+  // Without full rounds every CTA is idle and W = kTailSplit.
   const int nitems = Hq * ntiles;
   const int tS = (int)gridDim.x, tF = nitems / tS, tR = nitems - tF * tS;
   auto split_of = [&](int W, int& w, int& x) {  // parts per tail item under cap W: w, +1 for q < x
@@ -322,26 +348,50 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
   int tW = 1, tX = 0;
   if (mode == kTail && tR > 0) {
     int cap = kTailSplit;
-    if (tF > 0) {  // every thread estimates some CTAs' finish under each cap; the block takes the max
+    if (tF > 0) {
+      // a / b for the small non-negative operands here (< 2^22): float reciprocal, then one
+      // correction step (integer division by a runtime value is a long dependent sequence)
+      auto fdiv = [](int a, int b, float inv_b) {
+        int d = (int)((float)a * inv_b);
+        d += (d + 1) * b <= a;
+        d -= d * b > a;
+        return d;
+      };
+      const float inv_hq = 1.f / (float)Hq;
+      auto div_hq = [&](int i) { return fdiv(i, Hq, inv_hq); };
+      // full-round units of every CTA (into the stream-K prefix table, unused by kTail)
       for (int cx = tid; cx < tS; cx += kThreadsTC) {
         int L = 0;
         for (int k = 0; k < tF; ++k)
-          L += s_tsteps[ntiles - 1 - (k * tS + ((k & 1) ? tS - 1 - cx : cx)) / Hq] + kPieceCost;
-        const int rk = (tF & 1) ? tS - 1 - cx : cx;
-#pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          int w, x;
-          split_of(1 << e, w, x);
-          const int hi = x * (w + 1), q = rk < hi ? rk / (w + 1) : x + (rk - hi) / w;
-          int fin = L;
+          L += s_tsteps[ntiles - 1 - div_hq(k * tS + ((k & 1) ? tS - 1 - cx : cx))] + kPieceCost;
+        s_tpre[cx] = L;
+      }
+      __syncthreads();
+      // warps 2e and 2e + 1 estimate every CTA's finish under cap 2^e; one shared atomic per warp
+      if (warp < 8) {
+        const int e = warp >> 1;
+        int w, x;
+        split_of(1 << e, w, x);
+        const int hi = x * (w + 1);
+        const float inv_w = 1.f / (float)w, inv_w1 = 1.f / (float)(w + 1);
+        int fmax = 0;
+        for (int cx = (warp & 1) * 32 + lane; cx < tS; cx += 64) {
+          const int rk = (tF & 1) ? tS - 1 - cx : cx;
+          const int q = rk < hi ? fdiv(rk, w + 1, inv_w1) : x + fdiv(rk - hi, w, inv_w);
+          int fin = s_tpre[cx];
           if (q < tR) {
-            const int wq = w + (q < x ? 1 : 0), p = rk - (q * w + min(q, x));
-            const int n = s_tsteps[ntiles - 1 - (tF * tS + q) / Hq];
-            const int part = (p + 1) * n / wq - p * n / wq;
+            const bool big = q < x;
+            const int wq = big ? w + 1 : w, p = rk - (q * w + min(q, x));
+            const float inv_wq = big ? inv_w1 : inv_w;
+            const int n = s_tsteps[ntiles - 1 - div_hq(tF * tS + q)];
+            const int part = fdiv((p + 1) * n, wq, inv_wq) - fdiv(p * n, wq, inv_wq);
             if (part > 0) fin += part + kPieceCost + (part < n ? kMergeCost : 0);
           }
-          atomicMax(&s_fin[e], fin);
+          fmax = max(fmax, fin);
         }
+#pragma unroll
+        for (int o = 16; o; o >>= 1) fmax = max(fmax, __shfl_xor_sync(0xffffffffu, fmax, o));
+        if (lane == 0) atomicMax(&s_fin[e], fmax);
       }
       __syncthreads();
       cap = 1;
@@ -542,7 +592,7 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
     unsigned char* slots = ws ? ws + kCounterBytes : nullptr;
     // bounded barriers among softmax warps (an aborting warp never strands a partner): arrive,
     // then wait for the phase this thread's own count says is next
-    uint32_t quad_phase = 0, soft_phase = 0;
+    uint32_t quad_phase = 0, soft_phase = 0, bulk_phase = 0;
     auto quad_sync = [&]() -> bool {
       mbar_arrive(&quad_bar[quad]);
       return __all_sync(0xffffffffu, wait(&quad_bar[quad], (quad_phase++) & 1));
@@ -744,8 +794,41 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
         if (plan.seg(cx) == plan.seg(cx + 1)) return nullptr;
         return slots + (size_t)plan.slot_of(pm.item, cx) * kSlotBytes;
       };
+      // the pieces' O, three slots at a time, bulk-copied into the (now idle) Q/K/V tile buffers: one
+      // round trip per batch instead of one per slot; the first batch goes out before the maxima
+      constexpr int kBatch = kTilesBytes / (kRows * kD * 4);
+      auto issue_batch = [&](int base) {
+        if (tid != 0) return;
+        const unsigned char* src[kBatch];
+        uint32_t bytes = 0;
+#pragma unroll
+        for (int u = 0; u < kBatch; ++u) {
+          src[u] = base + u <= c_hi ? slot_at(base + u) : nullptr;
+          bytes += src[u] ? kRows * kD * 4 : 0;
+        }
+        // order this thread's acquired view of the partials and the previous batch's reads of the
+        // buffers (generic proxy) before the bulk copies (async proxy)
+        asm volatile("fence.proxy.async;" ::: "memory");
+        mbar_expect_tx(bulk_bar, bytes);
+#pragma unroll
+        for (int u = 0; u < kBatch; ++u)
+          if (src[u]) bulk_load(smem + (size_t)u * kRows * kD * 4, src[u], kRows * kD * 4, bulk_bar);
+      };
+      issue_batch(c_lo);
+      // maxima and sums of the first 8 slots, kept for the weights; further slots (stream-K only)
+      // 8 maxima at a time, their sums read again with their batch
+      float m8[8], l8[8];
+#pragma unroll
+      for (int u = 0; u < 8; ++u) {
+        const unsigned char* sl = c_lo + u <= c_hi ? slot_at(c_lo + u) : nullptr;
+        const float* mlx = sl ? reinterpret_cast<const float*>(sl + (size_t)kRows * kD * 4) : nullptr;
+        m8[u] = mlx ? __ldcg(mlx + trow) : -INFINITY;
+        l8[u] = mlx ? __ldcg(mlx + kRows + trow) : 0.f;
+      }
       float Mx = -INFINITY;
-      for (int base = c_lo; base <= c_hi; base += 8) {  // 8 slots' maxima in flight together
+#pragma unroll
+      for (int u = 0; u < 8; ++u) Mx = fmaxf(Mx, m8[u]);
+      for (int base = c_lo + 8; base <= c_hi; base += 8) {
         float mv[8];
 #pragma unroll
         for (int u = 0; u < 8; ++u) {
@@ -758,25 +841,49 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
       float acc[kColsPerWarp], den = 0.f;
 #pragma unroll
       for (int j = 0; j < kColsPerWarp; ++j) acc[j] = 0.f;
-      for (int cx = c_lo; cx <= c_hi; ++cx) {
-        const unsigned char* sl = slot_at(cx);
-        if (!sl) continue;
-        const float* mlx = reinterpret_cast<const float*>(sl + (size_t)kRows * kD * 4);
-        const float mk = __ldcg(mlx + trow), lk = __ldcg(mlx + kRows + trow);
-        float4 x[kColsPerWarp / 4];  // all of this piece's loads in flight together
-        const float4* src = reinterpret_cast<const float4*>(sl) + (size_t)(col / 4) * kRows + trow;
+      for (int base = c_lo; ok && base <= c_hi; base += kBatch) {
+        const unsigned char* sl[kBatch];
+        float mk[kBatch], lk[kBatch];
 #pragma unroll
-        for (int j = 0; j < kColsPerWarp / 4; ++j) x[j] = __ldcg(src + (size_t)j * kRows);
-        const float wk = mk == -INFINITY ? 0.f : ex2(mk - Mx);
-        den += wk * lk;
+        for (int u = 0; u < kBatch; ++u) {
+          sl[u] = base + u <= c_hi ? slot_at(base + u) : nullptr;
+          const int rel = base - c_lo + u;
+          if (rel < 8) {  // from the registers above (a select chain: the index is not a constant)
+            mk[u] = m8[0];
+            lk[u] = l8[0];
 #pragma unroll
-        for (int j = 0; j < kColsPerWarp / 4; ++j) {
-          acc[4 * j] = fmaf(x[j].x, wk, acc[4 * j]);
-          acc[4 * j + 1] = fmaf(x[j].y, wk, acc[4 * j + 1]);
-          acc[4 * j + 2] = fmaf(x[j].z, wk, acc[4 * j + 2]);
-          acc[4 * j + 3] = fmaf(x[j].w, wk, acc[4 * j + 3]);
+            for (int k = 1; k < 8; ++k) {
+              mk[u] = rel == k ? m8[k] : mk[u];
+              lk[u] = rel == k ? l8[k] : lk[u];
+            }
+            if (!sl[u]) mk[u] = -INFINITY, lk[u] = 0.f;
+          } else {
+            const float* mlx = sl[u] ? reinterpret_cast<const float*>(sl[u] + (size_t)kRows * kD * 4) : nullptr;
+            mk[u] = mlx ? __ldcg(mlx + trow) : -INFINITY;
+            lk[u] = mlx ? __ldcg(mlx + kRows + trow) : 0.f;
+          }
         }
+        ok = __all_sync(0xffffffffu, wait(bulk_bar, (bulk_phase++) & 1));
+        if (!ok) break;
+#pragma unroll
+        for (int u = 0; u < kBatch; ++u) {
+          if (!sl[u]) continue;
+          const float wk = mk[u] == -INFINITY ? 0.f : ex2(mk[u] - Mx);
+          den += wk * lk[u];
+          const float4* src = reinterpret_cast<const float4*>(smem + (size_t)u * kRows * kD * 4) + (col / 4) * kRows + trow;
+#pragma unroll
+          for (int j = 0; j < kColsPerWarp / 4; ++j) {
+            const float4 x = src[j * kRows];
+            acc[4 * j] = fmaf(x.x, wk, acc[4 * j]);
+            acc[4 * j + 1] = fmaf(x.y, wk, acc[4 * j + 1]);
+            acc[4 * j + 2] = fmaf(x.z, wk, acc[4 * j + 2]);
+            acc[4 * j + 3] = fmaf(x.w, wk, acc[4 * j + 3]);
+          }
+        }
+        ok = soft_sync();  // the batch is read: the next may overwrite the buffers
+        if (ok && base + kBatch <= c_hi) issue_batch(base + kBatch);
       }
+      if (!ok) break;
       if (row < R) {
         const float inv = den > 0.f ? 1.f / den : 0.f;
         T* orow = out + ((long long)row * Hq + it.head) * kD + col;
@@ -798,7 +905,7 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
     // an async unit arrives on gets a short bounded wait on both parities
     for (int b = 0; b < 2; ++b)
       for (int i = 0; i < kNumBars; ++i)
-        if (i < 10 || (i >= 13 && i < 19)) mbar_wait(bars + i, b, kAbortWaitNs);
+        if (i < 10 || (i >= 13 && i < 19) || i == 24) mbar_wait(bars + i, b, kAbortWaitNs);
   }
   __syncthreads();
   if (warp == 0) {
