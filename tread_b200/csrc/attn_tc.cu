@@ -529,9 +529,17 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
       const int b = (int)(g & 1);
       const uint64_t vb = dv0 + (uint64_t)b * kStage;
 #pragma unroll
-      for (int kk = 0; kk < kKeys / 16; ++kk)
-        mma_f16_ts_elect(tmem + kTmemO + (kk >> 2) * 128, tmem + b * kKeys + (kk >> 2) * 64 + (kk & 3) * 8,
-                         vb + (uint64_t)((kk * 16 * 128) >> 4), idesc_pv, (!fresh || (kk & 3) > 0) ? 1u : 0u);
+      for (int h = 0; h < 2; ++h) {  // one group of four per key half
+        uint32_t ta[4];
+        uint64_t vd[4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const int kk = 4 * h + i;
+          ta[i] = tmem + b * kKeys + h * 64 + i * 8;
+          vd[i] = vb + (uint64_t)((kk * 16 * 128) >> 4);
+        }
+        mma_f16_ts_x4_elect(tmem + kTmemO + h * 128, ta, vd, idesc_pv, fresh ? 0u : 1u);
+      }
       mma_commit_elect(&pv_done[b]);
       mma_commit_elect(&v_free[b]);
     };
@@ -564,10 +572,15 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
         if (!ok) break;
         tc_fence_after();
         const uint64_t kb = dk0 + (uint64_t)s * kStage;
+        {
+          uint64_t ad[8], bd[8];
 #pragma unroll
-        for (int kk = 0; kk < kD / 16; ++kk) {
-          const uint64_t off = (uint64_t)(((kk >> 2) * kBlock + (kk & 3) * 32) >> 4);
-          mma_f16_elect(tmem + s * kKeys, dqk + off, kb + off, idesc_qk, kk > 0);
+          for (int kk = 0; kk < kD / 16; ++kk) {
+            const uint64_t off = (uint64_t)(((kk >> 2) * kBlock + (kk & 3) * 32) >> 4);
+            ad[kk] = dqk + off;
+            bd[kk] = kb + off;
+          }
+          mma_f16_x8_elect(tmem + s * kKeys, ad, bd, idesc_qk, 0u);
         }
         mma_commit_elect(&s_full[s]);
         mma_commit_elect(&k_free[s]);

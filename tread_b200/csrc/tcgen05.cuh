@@ -116,6 +116,47 @@ __device__ __forceinline__ void mma_f16_ts_elect(uint32_t tmem_d, uint32_t tmem_
       : "memory");
 }
 
+// Eight MMAs into one accumulator from one elected lane in one block: the first accumulates iff
+// `acc`, the rest always (the K = 128 of a 128-key step as eight K = 16 instructions).
+__device__ __forceinline__ void mma_f16_x8_elect(uint32_t tmem_d, const uint64_t (&a)[8], const uint64_t (&b)[8],
+                                                 uint32_t idesc, uint32_t acc) {
+  asm volatile(
+      "{\n\t.reg .pred p, t, e;\n\t"
+      "elect.sync _|e, 0xffffffff;\n\t"
+      "setp.ne.b32 p, %2, 0;\n\t"
+      "setp.eq.b32 t, %2, %2;\n\t"
+      "@e tcgen05.mma.cta_group::1.kind::f16 [%0], %3, %11, %1, p;\n\t"
+      "@e tcgen05.mma.cta_group::1.kind::f16 [%0], %4, %12, %1, t;\n\t"
+      "@e tcgen05.mma.cta_group::1.kind::f16 [%0], %5, %13, %1, t;\n\t"
+      "@e tcgen05.mma.cta_group::1.kind::f16 [%0], %6, %14, %1, t;\n\t"
+      "@e tcgen05.mma.cta_group::1.kind::f16 [%0], %7, %15, %1, t;\n\t"
+      "@e tcgen05.mma.cta_group::1.kind::f16 [%0], %8, %16, %1, t;\n\t"
+      "@e tcgen05.mma.cta_group::1.kind::f16 [%0], %9, %17, %1, t;\n\t"
+      "@e tcgen05.mma.cta_group::1.kind::f16 [%0], %10, %18, %1, t;\n\t"
+      "}"
+      ::"r"(tmem_d), "r"(idesc), "r"(acc), "l"(a[0]), "l"(a[1]), "l"(a[2]), "l"(a[3]), "l"(a[4]), "l"(a[5]), "l"(a[6]),
+      "l"(a[7]), "l"(b[0]), "l"(b[1]), "l"(b[2]), "l"(b[3]), "l"(b[4]), "l"(b[5]), "l"(b[6]), "l"(b[7])
+      : "memory");
+}
+// Four MMAs into one accumulator with A (P) in tensor memory at a[i], from one elected lane; the
+// first accumulates iff `acc`, the rest always.
+__device__ __forceinline__ void mma_f16_ts_x4_elect(uint32_t tmem_d, const uint32_t (&a)[4], const uint64_t (&b)[4],
+                                                    uint32_t idesc, uint32_t acc) {
+  asm volatile(
+      "{\n\t.reg .pred p, t, e;\n\t"
+      "elect.sync _|e, 0xffffffff;\n\t"
+      "setp.ne.b32 p, %2, 0;\n\t"
+      "setp.eq.b32 t, %2, %2;\n\t"
+      "@e tcgen05.mma.cta_group::1.kind::f16 [%0], [%3], %7, %1, p;\n\t"
+      "@e tcgen05.mma.cta_group::1.kind::f16 [%0], [%4], %8, %1, t;\n\t"
+      "@e tcgen05.mma.cta_group::1.kind::f16 [%0], [%5], %9, %1, t;\n\t"
+      "@e tcgen05.mma.cta_group::1.kind::f16 [%0], [%6], %10, %1, t;\n\t"
+      "}"
+      ::"r"(tmem_d), "r"(idesc), "r"(acc), "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "l"(b[0]), "l"(b[1]), "l"(b[2]),
+      "l"(b[3])
+      : "memory");
+}
+
 __device__ __forceinline__ void mma_commit_elect(uint64_t* bar) {
   asm volatile(
       "{\n\t.reg .pred e;\n\t"
