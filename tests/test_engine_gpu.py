@@ -305,7 +305,8 @@ def _sdpa_ref(q, K, V, pos):
     return o.transpose(0, 1)
 
 
-# variants of the tensor-core kernel: the default choice, the stream-K schedule forced, one whole
+# variants of the tensor-core kernel: the default choice (tail split with a workspace), the stream-K
+# and tail-split schedules forced, one whole
 # row tile per CTA (no workspace)
 VARIANTS = {"default": {}, "stream_k": dict(schedule="stream_k"), "tail_split": dict(schedule="tail_split"),
             "whole_tiles": dict(workspace=False)}
@@ -345,7 +346,7 @@ def test_tensor_core_attention_matches_fp32_reference(cuda, dtype, R, Hq, Hkv, T
 @pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
 @pytest.mark.parametrize("case", ["causal_prefill", "unsorted", "query_only", "one_row"])
 def test_tensor_core_attention_schedules(cuda, dtype, case):
-    """Shapes that stress the stream-K split and merge: a causal prefill of 8000 rows (the deviation
+    """Shapes that stress the split schedules and merges: a causal prefill of 8000 rows (the deviation
     pass's layer 0: tiles of 1..63 key blocks), rows in random order (a tile's length is its latest
     row), 64 query rows only (14 pairs split over every SM), a single row."""
     gen = torch.Generator(device=cuda).manual_seed(7)
@@ -367,6 +368,25 @@ def test_tensor_core_attention_schedules(cuda, dtype, case):
     K = torch.randn(Hkv, T, D, device=cuda, generator=gen).to(dtype)
     V = torch.randn(Hkv, T, D, device=cuda, generator=gen).to(dtype)
     _check_attention(cuda, dtype, q, K, V, pos)
+
+
+@pytest.mark.parametrize("items,T", [("S-1", 2048), ("S", 2048), ("S+1", 2048), ("2S", 1000), ("2S+1", 1000),
+                                     ("S/3", 300)])
+def test_tensor_core_attention_tail_rounds(cuda, items, T):
+    """Tile counts around multiples of the SM count S (one head, so tiles = items): no full round,
+    exactly one or two full rounds and nothing left, one tile left after one round (where the
+    split cap is estimated), and tiles of 3 key blocks split up to 8 ways (empty parts). The
+    last tile is partly filled."""
+    S = torch.cuda.get_device_properties(cuda).multi_processor_count
+    n = {"S-1": S - 1, "S": S, "S+1": S + 1, "2S": 2 * S, "2S+1": 2 * S + 1, "S/3": S // 3}[items]
+    gen = torch.Generator(device=cuda).manual_seed(n + T)
+    R, D = n * 128 - 5, 128
+    q = torch.randn(R, 1, D, device=cuda, generator=gen).to(torch.bfloat16)
+    K = torch.randn(1, T, D, device=cuda, generator=gen).to(torch.bfloat16)
+    V = torch.randn(1, T, D, device=cuda, generator=gen).to(torch.bfloat16)
+    pos = torch.randint(0, T, (R,), device=cuda, generator=gen).sort().values
+    _check_attention(cuda, torch.bfloat16, q, K, V, pos,
+                     variants={k: VARIANTS[k] for k in ("default", "tail_split", "stream_k")})
 
 
 def test_tensor_core_attention_flags_out_of_range_positions(cuda):

@@ -329,7 +329,7 @@ _attn_ws = {}
 
 
 def attn_workspace(device):
-    """The zero-filled stream-K workspace of tread_attn_rows on `device` (allocated once, then kept:
+    """The zero-filled split-tile workspace of tread_attn_rows on `device` (allocated once, then kept:
     captured CUDA graphs hold its address). Calls sharing it must be stream-ordered."""
     idx = torch.device(device).index
     ws = _attn_ws.get(idx)

@@ -150,7 +150,7 @@ class Qwen2Rows:
         if e:
             self.err.zero_()
             sel.zero_()
-            if e & 4:  # an attention kernel gave up on a wait: its stream-K counters may be stale
+            if e & 4:  # an attention kernel gave up on a wait: its split-tile counters may be stale
                 kernels.reset_attn_workspace(self.device)
             raise RuntimeError(f"tread_b200 kernel reported an error (flags {e:#x}: 1, 2 out-of-range position, "
                                f"4 wait timeout)")
