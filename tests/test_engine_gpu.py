@@ -306,8 +306,7 @@ def _sdpa_ref(q, K, V, pos):
 
 
 # variants of the tensor-core kernel: the default choice (tail split with a workspace), the stream-K
-# and tail-split schedules forced, one whole
-# row tile per CTA (no workspace)
+# and tail-split schedules forced, one whole row tile per CTA (no workspace)
 VARIANTS = {"default": {}, "stream_k": dict(schedule="stream_k"), "tail_split": dict(schedule="tail_split"),
             "whole_tiles": dict(workspace=False)}
 
