@@ -4,18 +4,20 @@
 // forward of tread/engine.py:131-132): row r of head h attends to every cache key at a position
 // <= pos[r] of KV head h / (Hq/Hkv). This path covers bf16/fp16 with head_dim 128.
 //
-// Work items and schedule. An item is a tile of 128 consecutive rows of one query head; it takes
-// n = (latest position among its rows) / 128 + 1 key blocks ("steps"). With a workspace, all
-// items' steps are laid end to end (items of one KV head together, for L2 reuse of its K/V) and
-// cut into one equal contiguous segment per CTA, one CTA per SM (stream-K): a CTA runs the pieces
-// of items in its segment one after another, and an item cut between CTAs leaves partial results
-// (unnormalised O, running max m and sum l per row) in the workspace; after its last piece a CTA
-// counts its (at most two) partial pieces in, and the one that completes an item (an atomic
-// count per item, no waiting) merges its partials:
+// Work items and schedules. An item is a tile of 128 consecutive rows of one query head; it takes
+// n = (latest position among its rows) / 128 + 1 key blocks ("steps"). A CTA runs its pieces (an
+// item's whole key range or a contiguous part of it) one after another.
+//   - tail split (default with a workspace): one CTA per SM; full rounds of whole items, longest
+//     first, in snake order, then the items left over split by key range over all CTAs (the
+//     split cap chosen by an estimate of every CTA's finish; details at the plan below);
+//   - stream-K (on request): all items' steps laid end to end (items of one KV head together, for
+//     L2 reuse of its K/V) and cut into one equal contiguous segment per CTA;
+//   - whole tiles (no workspace): one CTA per item, latest rows first.
+// An item cut between CTAs leaves partial results (unnormalised O, running max m and sum l per
+// row) in the workspace; after its last piece a CTA counts its (at most two) partial pieces in,
+// and the one that completes an item (an atomic count per item, no waiting) merges its partials,
+// bulk-copied into its idle tile buffers:
 //     O = sum_k O_k 2^(m_k - M) / sum_k l_k 2^(m_k - M),  M = max_k m_k.
-// The schedule is used when the tiles do not fill one wave of SMs (the query rows alone); with
-// more tiles, or without a workspace, every CTA runs one whole tile, latest rows first (the
-// measured trade-off is at the launch site).
 //
 // Roles and pipeline per CTA:
 //   - loader (lane 0 of warp 9): TMA (128-byte swizzle) loads each piece's Q tile and 128-key K
@@ -28,7 +30,8 @@
 //     O_h += P_g[:, half h] V_g[half h, :], with P read from TMEM;
 //   - softmax (warps 0-7; a row = a TMEM lane, its 128 key columns split into two halves, one per
 //     warp): reads its half of S once, masks keys past the row's position, keeps the half's own
-//     running max and sum in the exp2 domain (ex2.approx on MUFU), rescales the half's O in TMEM
+//     running max and sum in the exp2 domain (ex2.approx on the MUFU, a share of the pairs as a
+//     cubic on the FMA pipe), rescales the half's O in TMEM
 //     only when its max grows by more than 8 (a stale max is exact since 1/l uses the same max; a
 //     warp decides together because tcgen05.ld/st are warp-collective), and writes P over the S
 //     columns it has just read. The halves are merged once per piece, in the epilogue.
