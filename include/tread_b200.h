@@ -38,7 +38,8 @@ enum { TREAD_F32 = 0, TREAD_F16 = 1, TREAD_BF16 = 2 };
 /* Text of the last error raised on the calling host thread ("" if none). */
 const char* tread_last_error(void);
 
-/* ABI revision of this library; bumped on any signature change. */
+/* ABI revision of this library; bumped on any signature change or newly accepted flag (4: tread_attn_rows
+ * accepts TREAD_ATTN_FORCE_TAIL_SPLIT). */
 int tread_abi_version(void);
 
 /*
