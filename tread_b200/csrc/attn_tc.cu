@@ -682,6 +682,8 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
           const float2 pp = (i % 16) < 2 * kPolyPairs ? exp2_poly2(x) : make_float2(ex2(x.x), ex2(x.y));
           l2 = fadd2(l2, pp);
           pk[i / 2] = pack2<T>(pp.x, pp.y);
+          // the first half of P goes out while the second half is computed
+          if (i == kColsPerWarp / 2 - 2) tmem_st16u(tmem + s * kKeys + part * 64 + lane_off, pk);
         }
         l += l2.x + l2.y;
         // this half's O must be stable (PV(g-1) complete) to rescale it; tcgen05.ld/st are
@@ -700,7 +702,7 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
           }
         }
         // P over this warp's own S columns (already in registers): QK(g+2) waits for PV(g)
-        tmem_st32u(tmem + s * kKeys + part * 64 + lane_off, pk);
+        tmem_st16u(tmem + s * kKeys + part * 64 + 16 + lane_off, pk + 16);
         asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
         tc_fence_before();
         mbar_arrive(&p_full[s]);
