@@ -972,7 +972,9 @@ def load_peaks():
 def run_e2e(args, dev, pool_k, pool_v, ids, deltas, inv, world, rank):
     """Host buffers in and out: per step, fetch the 16 blocks from pinned host memory, rotate and
     append each as soon as it lands, and copy each block's slice of the assembled cache back to
-    pinned host memory; three streams pipeline H2D, kernel and D2H per block."""
+    pinned host memory; three streams pipeline H2D, kernel and D2H per block. The device-side
+    assembled cache alternates between two buffers by step, so a block's kernel in step s+1 never
+    waits for step s's copy-out of the same rows; H2D and D2H stay busy together."""
     from tread_b200 import kernels
 
     nblk = args.blocks
@@ -980,8 +982,9 @@ def run_e2e(args, dev, pool_k, pool_v, ids, deltas, inv, world, rank):
     host_k = [pool_k[i].cpu().pin_memory() for i in range(nhost)]
     host_v = [pool_v[i].cpu().pin_memory() for i in range(nhost)]
     T = nblk * NTOK
-    out_k = torch.empty((L, 1, HKV, T, D), device=dev, dtype=torch.bfloat16)
-    out_v = torch.empty_like(out_k)
+    outs = [(torch.empty((L, 1, HKV, T, D), device=dev, dtype=torch.bfloat16),
+             torch.empty((L, 1, HKV, T, D), device=dev, dtype=torch.bfloat16)) for _ in range(2)]
+    out_k, out_v = outs[0]
     hout_k = torch.empty(out_k.shape, dtype=torch.bfloat16).pin_memory()
     hout_v = torch.empty(out_v.shape, dtype=torch.bfloat16).pin_memory()
     stage_k = [torch.empty((L, 1, HKV, NTOK, D), device=dev, dtype=torch.bfloat16) for _ in range(nblk)]
@@ -989,10 +992,10 @@ def run_e2e(args, dev, pool_k, pool_v, ids, deltas, inv, world, rank):
     s_in, s_cmp, s_out = torch.cuda.Stream(dev), torch.cuda.Stream(dev), torch.cuda.Stream(dev)
     ev_in = [torch.cuda.Event() for _ in range(nblk)]
     ev_cmp = [torch.cuda.Event() for _ in range(nblk)]
-    ev_out = [torch.cuda.Event() for _ in range(nblk)]
+    ev_out = [[torch.cuda.Event() for _ in range(nblk)] for _ in range(2)]  # by output buffer
     nsteps = 2 + args.e2e_steps
     plans = [[kernels.RopeAppendPlan([(stage_k[j], stage_v[j], int(deltas[s % len(deltas)][j]), j * NTOK)],
-                                     out_k, out_v, inv) for j in range(nblk)] for s in range(nsteps)]
+                                     outs[s % 2][0], outs[s % 2][1], inv) for j in range(nblk)] for s in range(nsteps)]
     launches = 0
 
     def step(s):
@@ -1004,14 +1007,15 @@ def run_e2e(args, dev, pool_k, pool_v, ids, deltas, inv, world, rank):
             kernels.kv_fetch(stage_v[j], host_v[i], s_in)
             ev_in[j].record(s_in)
             s_cmp.wait_event(ev_in[j])
-            s_cmp.wait_event(ev_out[j])  # previous step's D2H of these rows finished
+            s_cmp.wait_event(ev_out[s % 2][j])  # step s-2's D2H of these rows of this buffer finished
             plans[s][j].launch(s_cmp)
             launches += 1
             ev_cmp[j].record(s_cmp)
             s_out.wait_event(ev_cmp[j])
-            kernels.kv_spill_rows(hout_k, out_k, j * NTOK, NTOK, s_out)
-            kernels.kv_spill_rows(hout_v, out_v, j * NTOK, NTOK, s_out)
-            ev_out[j].record(s_out)
+            ok_, ov_ = outs[s % 2]
+            kernels.kv_spill_rows(hout_k, ok_, j * NTOK, NTOK, s_out)
+            kernels.kv_spill_rows(hout_v, ov_, j * NTOK, NTOK, s_out)
+            ev_out[s % 2][j].record(s_out)
 
     for s in range(2):
         step(s)
