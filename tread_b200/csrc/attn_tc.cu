@@ -101,9 +101,9 @@ constexpr int kTilesBytes = 12 * kBlock;
 constexpr int kSmem = 1024 + kTilesBytes + 8 * kMaxTiles + 512;
 // Stream-K cost of an item's start and end (pipeline fill and drain, epilogue), in steps.
 constexpr int kPieceCost = 3;
-// Exponentials per 16 keys of a softmax lane that run as a polynomial on the FMA pipe instead of
-// the MUFU (in pairs): the MUFU's 16 ex2 per clock per SM would otherwise take as long per step as
-// the two 128-cube MMAs.
+// Exponentials per 16 keys of a softmax lane computed as a polynomial on the FMA pipe instead of
+// ex2 on the MUFU (in pairs). Measured on B200, 2 of every 8 pairs is fastest: the softmax step is
+// latency-bound, and the polynomial shortens its chains of dependent exponentials.
 #ifndef TREAD_ATTN_POLY_PAIRS
 #define TREAD_ATTN_POLY_PAIRS 2
 #endif
@@ -970,9 +970,10 @@ int launch_tc(const void* q, const void* K, const void* V, long long c_sh, long 
   const long long nitems = (long long)Hq * ntiles;
   const int sms = sm_count();
   // Schedule (measured on B200): with a workspace, persistent CTAs (one per SM) over whole tiles,
-  // longest first, the tiles left after the full rounds split into key ranges (kTail); it beats
-  // both one CTA per tile and stream-K from 64 rows to 8000. Without a workspace, one CTA per whole
-  // tile. force (kStreamK / kTail, from the caller's flags) overrides the choice.
+  // longest first, the tiles left after the full rounds split into key ranges (kTail). From 64
+  // rows to 8000 it is as fast as one CTA per tile or faster (up to 2x for few tiles), and faster
+  // than stream-K. Without a workspace, one CTA per whole tile. force (kStreamK / kTail, from the
+  // caller's flags) overrides the choice.
   const bool ws_ok = ws != nullptr && ws_bytes >= kCounterBytes + (size_t)2 * sms * kSlotBytes &&
                      nitems <= kMaxItems && ntiles <= kMaxTiles && T_cache <= (1LL << 24);
   const int mode = !ws_ok ? kWhole : force ? force : kTail;
