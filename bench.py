@@ -62,7 +62,7 @@ def parse():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=10.0, help="CPU baseline sample budget")
     ap.add_argument("--no-ttft", action="store_true", help="skip the configs[2] 7B TTFT leg")
-    ap.add_argument("--only", choices=["attention", "selector", "ttft"], default=None,
+    ap.add_argument("--only", choices=["attention", "selector", "ttft", "rows_gemm"], default=None,
                     help="run one kernel microbench alone (for profiler captures) and print its timing")
     ap.add_argument("--ttft-reps", type=int, default=5, help="timed warm requests per recompute ratio")
     ap.add_argument("--no-dp", action="store_true", help="skip the configs[4] hash-sharded replica serving leg")
@@ -1095,6 +1095,14 @@ def run_only(args):
         out = torch.empty_like(q)
         run = lambda: kernels.attn_rows(q, K, V, pos, out=out)
         flops = 4.0 * D * Hq * float((pos + 1).sum().item())
+    elif args.only == "rows_gemm":
+        # the query forward's gate/up projection of one 7B layer: 64 query rows, a 271.6 MB weight
+        # (larger than L2, so every call streams it from HBM)
+        x = torch.randn(nq, 3584, device=dev, generator=gen).to(torch.bfloat16)
+        w = (torch.randn(2 * 18944, 3584, device=dev, generator=gen) * 0.02).to(torch.bfloat16)
+        out = torch.empty(nq, w.shape[0], dtype=torch.bfloat16, device=dev)
+        run = lambda: kernels.rows_gemm(x, w, out=out)
+        flops = None
     else:
         n = 8192
         K1 = torch.randn(HKV, n, D, device=dev, generator=gen).to(torch.bfloat16)
@@ -1121,6 +1129,9 @@ def run_only(args):
     line = {"only": args.only, "us_per_call": round(us, 2)}
     if flops:
         line["tflops"] = round(flops / (us * 1e-6) / 1e12, 1)
+    if args.only == "rows_gemm":
+        gbs = w.numel() * 2 / (us * 1e-6) / 1e9
+        line.update(gbs=round(gbs, 1), frac_of_hbm=round(gbs / load_peaks()["hbm_gbs"], 3))
     print(json.dumps(line), flush=True)
     return 0
 

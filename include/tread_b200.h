@@ -38,8 +38,8 @@ enum { TREAD_F32 = 0, TREAD_F16 = 1, TREAD_BF16 = 2 };
 /* Text of the last error raised on the calling host thread ("" if none). */
 const char* tread_last_error(void);
 
-/* ABI revision of this library; bumped on any signature change or newly accepted flag (4: tread_attn_rows
- * accepts TREAD_ATTN_FORCE_TAIL_SPLIT). */
+/* ABI revision of this library; bumped on any signature change, new entry point or newly accepted flag
+ * (4: tread_attn_rows accepts TREAD_ATTN_FORCE_TAIL_SPLIT; 5: tread_rows_gemm). */
 int tread_abi_version(void);
 
 /*
@@ -231,6 +231,27 @@ int tread_rmsnorm(const void* x, int64_t ld_x, const void* weight, void* y, int6
  */
 int tread_silu_mul(const void* gate_up, int64_t ld_gu, void* y, int64_t ld_y, int64_t rows, int inter,
                    int dtype, tread_stream_t stream);
+
+/*
+ * Few-row projection GEMM on the tensor cores:
+ *   out[M, N] = (accumulate ? out : 0) + x[M, K] w[N, K]^T + bias[N]
+ * fp32 accumulation, rounded once to dtype. It replaces the Linear layers of the query forward when
+ * only the query segment's rows run (tread/engine.py:131-132: the q/k/v, o_proj, gate/up, down
+ * projections and lm_head of model(query_ids, past_key_values=cache)); there the weights dominate
+ * the traffic and the GEMM is bound by HBM. 1 <= M <= 128.
+ * bf16 / fp16 only. x, w, out: row-major at row strides ldx, ldw, ld_out (elements). x and w must be
+ * 16-byte aligned, and K, ldx and ldw multiples of 8. bias (length N) may be NULL. out must not
+ * overlap x or w.
+ * workspace: NULL, or tread_rows_gemm_workspace_bytes() of device memory, 256-byte aligned (its
+ * contents on entry do not matter). With it, weights with fewer 256-feature pairs than SMs are split
+ * along K over more CTAs, and a second launch adds the splits' partial sums in split order, so the
+ * result does not depend on timing. Calls that share a workspace must be stream-ordered. A bounded
+ * wait that gives up sets bit 2 of *err_flag (may be NULL).
+ */
+size_t tread_rows_gemm_workspace_bytes(void);
+int tread_rows_gemm(const void* x, int64_t ldx, const void* w, int64_t ldw, const void* bias, void* out,
+                    int64_t ld_out, int M, int N, int K, int accumulate, int dtype, void* err_flag,
+                    void* workspace, size_t workspace_bytes, tread_stream_t stream);
 
 /*
  * Block-store tier transfers (pinned host <-> HBM), stream-ordered DMA copies.

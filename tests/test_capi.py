@@ -205,3 +205,26 @@ def test_silu_mul_rejects_bad_arguments(over, needle):
     rc = C.lib().tread_silu_mul(a["gu"], a["ld"], a["y"], a["ldy"], a["rows"], a["inter"], a["dtype"], None)
     assert rc == 1
     assert needle in C.lib().tread_last_error().decode()
+
+
+@pytest.mark.parametrize("over,needle", [
+    (dict(M=129), "rows above"), (dict(K=0), "K == 0"), (dict(x=0), "null"), (dict(dtype=C.TREAD_F32), "dtype"),
+    (dict(x=264), "aligned"), (dict(ldx=60), "row stride"), (dict(K=60, ldx=64, ldw=64), "multiples of 8"),
+    (dict(ldw=68), "multiples of 8"), (dict(ws=512 + 64), "256-byte"),
+])
+def test_rows_gemm_rejects_bad_arguments(over, needle):
+    a = dict(x=256, ldx=64, w=256, ldw=64, bias=None, out=256, ldo=128, M=4, N=128, K=64, acc=0,
+             dtype=C.TREAD_BF16, ws=None)
+    a.update(over)
+    rc = C.lib().tread_rows_gemm(a["x"], a["ldx"], a["w"], a["ldw"], a["bias"], a["out"], a["ldo"], a["M"], a["N"],
+                                 a["K"], a["acc"], a["dtype"], None, a["ws"], 0, None)
+    assert rc == 1
+    assert needle in C.lib().tread_last_error().decode()
+
+
+def test_rows_gemm_empty_is_noop():
+    assert C.lib().tread_rows_gemm(None, 0, None, 0, None, None, 0, 0, 16, 16, 0, C.TREAD_BF16, None, None, 0,
+                                   None) == 0
+    assert C.lib().tread_rows_gemm(None, 0, None, 0, None, None, 0, 4, 0, 16, 0, C.TREAD_BF16, None, None, 0,
+                                   None) == 0
+    assert C.lib().tread_rows_gemm_workspace_bytes() % 256 == 0

@@ -60,6 +60,12 @@ SIGNATURES = {
         [P, P, P, I64, I64, P, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int, F32, P, ctypes.c_int,
          ctypes.c_int, P, P, ctypes.c_size_t, P],
     ),
+    "tread_rows_gemm_workspace_bytes": (ctypes.c_size_t, []),
+    "tread_rows_gemm": (
+        ctypes.c_int,
+        [P, I64, P, I64, P, P, I64, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int, P, P,
+         ctypes.c_size_t, P],
+    ),
     "tread_rmsnorm": (ctypes.c_int, [P, I64, P, P, I64, I64, ctypes.c_int, F32, ctypes.c_int, P]),
     "tread_silu_mul": (ctypes.c_int, [P, I64, P, I64, I64, ctypes.c_int, ctypes.c_int, P]),
     "tread_kv_fetch": (ctypes.c_int, [P, P, ctypes.c_size_t, P]),

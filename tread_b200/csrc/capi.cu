@@ -16,4 +16,4 @@ void set_error(const char* fmt, ...) {
 
 extern "C" const char* tread_last_error(void) { return tread::g_last_error; }
 
-extern "C" int tread_abi_version(void) { return 4; }
+extern "C" int tread_abi_version(void) { return 5; }

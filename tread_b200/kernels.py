@@ -385,6 +385,82 @@ def attn_rows(q, K, V, pos, out=None, sm_scale=None, err=None, stream=None, cuda
     return out
 
 
+# ---- few-row projections on the tensor cores ----------------------------------------------------
+
+ROWS_GEMM_MAX_ROWS = 128
+_gemm_ws = {}
+
+
+def rows_gemm_workspace(device):
+    """The K-split workspace of tread_rows_gemm on `device` (allocated once, then kept: captured CUDA
+    graphs hold its address). Calls sharing it must be stream-ordered."""
+    idx = torch.device(device).index
+    ws = _gemm_ws.get(idx)
+    if ws is None:
+        with torch.cuda.device(device):
+            n = C.lib().tread_rows_gemm_workspace_bytes()
+        ws = torch.zeros(n, dtype=torch.uint8, device=device)
+        _gemm_ws[idx] = ws
+    return ws
+
+
+def rows_gemm_fits(x, w):
+    """True when x [M, K] @ w[N, K]^T can run on tread_rows_gemm: 1..128 rows, bf16 / fp16, unit
+    column strides, 16-byte aligned rows and K a multiple of 8."""
+    return (x.dim() == 2 and w.dim() == 2 and 0 < x.shape[0] <= ROWS_GEMM_MAX_ROWS and x.is_cuda
+            and x.dtype in (torch.bfloat16, torch.float16) and w.dtype == x.dtype and x.shape[1] == w.shape[1]
+            and x.stride(1) == 1 and w.stride(1) == 1 and x.shape[1] % 8 == 0 and x.stride(0) % 8 == 0
+            and w.stride(0) % 8 == 0 and x.data_ptr() % 16 == 0 and w.data_ptr() % 16 == 0)
+
+
+_sm_counts = {}
+
+
+def rows_gemm_streams_alone(w):
+    """True when w [N, K] has at least one pair of 128-feature tiles per SM, so tread_rows_gemm
+    streams it in one wave without a K split. Measured on B200 (CUDA-graph replay, 7B shapes),
+    those weights (gate/up: 37888 x 3584; lm_head: 151936 x 3584) run at 0.88-0.97 of the HBM copy
+    peak, 1-2 % ahead of cuBLAS. The narrower ones need a K split and a second launch, and lose
+    about 4 us to cuBLAS on a 26-33 MB weight."""
+    idx = w.device.index
+    n = _sm_counts.get(idx)
+    if n is None:
+        n = _sm_counts[idx] = torch.cuda.get_device_properties(w.device).multi_processor_count
+    return w.shape[0] >= 256 * n
+
+
+def rows_gemm(x, w, bias=None, out=None, accumulate=False, err=None, stream=None, split=True):
+    """out = (accumulate ? out : 0) + x @ w^T + bias for few rows (x [M <= 128, K], w [N, K], as a
+    Linear layer stores its weight), fp32 accumulation rounded once, on the tensor cores with the
+    weights streamed from HBM (the query forward's projections, tread/engine.py:131-132). With
+    `split` (default) weights with fewer 256-feature pairs than SMs are split along K over more CTAs
+    through the device's shared workspace; the splits are added in a fixed order, so results are
+    deterministic."""
+    C.require_cuda(x, "x")
+    if not rows_gemm_fits(x, w):
+        raise ValueError("rows_gemm: x [M <= 128, K] and w [N, K] must be bf16/fp16 with unit column strides, "
+                         "16-byte aligned rows and K % 8 == 0")
+    M, K = x.shape
+    N = w.shape[0]
+    if bias is not None and (bias.shape != (N,) or bias.dtype != x.dtype or not bias.is_contiguous()):
+        raise ValueError("rows_gemm: bias must be a contiguous [N] tensor of x's dtype")
+    if out is None:
+        if accumulate:
+            raise ValueError("rows_gemm: accumulate needs out")
+        out = torch.empty(M, N, dtype=x.dtype, device=x.device)
+    elif out.shape != (M, N) or out.dtype != x.dtype or out.stride(1) != 1:
+        raise ValueError("rows_gemm: out must be [M, N] of x's dtype with unit column stride")
+    ws = rows_gemm_workspace(x.device) if split else None
+    with torch.cuda.device(x.device):
+        rc = C.lib().tread_rows_gemm(x.data_ptr(), x.stride(0), w.data_ptr(), w.stride(0),
+                                     None if bias is None else bias.data_ptr(), out.data_ptr(), out.stride(0), M, N,
+                                     K, 1 if accumulate else 0, C.dtype_code(x.dtype),
+                                     None if err is None else err.data_ptr(), None if ws is None else ws.data_ptr(),
+                                     0 if ws is None else ws.numel(), _stream_arg(stream, x.device))
+    C.check(rc, "tread_rows_gemm")
+    return out
+
+
 # ---- fused row-wise layer pieces ----------------------------------------------------------------
 
 def rmsnorm(x, weight, eps, out=None, stream=None):

@@ -5,10 +5,13 @@ The reference drives HF's Qwen2 modules directly (tread/blend.py:82-114, tread/e
 that every path the hot path needs is one primitive: a set of token rows, each at its own
 absolute position, runs through layers [l0, l1) against per-layer KV caches, with
 
-    x = RMSNorm(h) (tread_rmsnorm);  qkv = x @ Wqkv^T + b  (one GEMM, cuBLAS)
+    x = RMSNorm(h) (tread_rmsnorm);  qkv = x @ Wqkv^T + b  (one GEMM)
     RoPE(q, k at pos) ; K[pos], V[pos] = k, v              (tread_rope_rows)
     o = attention(q, K, V, key_pos <= pos)                 (tread_attn_rows)
     h = h + o @ Wo^T ; h = h + down(silu(gate) * up)       (GEMMs; tread_silu_mul)
+
+GEMMs of up to 128 rows (the query segment alone) against the widest weights (gate/up, lm_head)
+stream those weights through tread_rows_gemm on the tensor cores; the rest run as cuBLAS GEMMs.
 
 Rows are: recomputed tokens (blend), the query segment, a prefix or a doc being prefilled.
 A row only ever sees keys at positions <= its own, which is the causal mask of a prefill, the
@@ -68,6 +71,8 @@ class Qwen2Rows:
                     wgu=wgu, wd=m.down_proj.weight, inter=inter,
                 ))
         self.err = torch.zeros(4, dtype=torch.int32, device=self.device)
+        if self.device.type == "cuda":
+            kernels.rows_gemm_workspace(self.device)  # before any graph capture holds its address
 
     # -- elementwise pieces (HF Qwen2RMSNorm / SwiGLU semantics, fused kernels) ------------------
     @staticmethod
@@ -77,10 +82,28 @@ class Qwen2Rows:
     def embed_ids(self, ids):
         return F.embedding(ids, self.embed)
 
+    @staticmethod
+    def linear(x, w, bias=None, out=None, accumulate=False):
+        """x @ w^T (+ bias), or out + x @ w^T in place when `accumulate`, rounded once (HF Linear /
+        torch.addmm). Up to 128 rows against a weight wide enough to fill every SM without a K
+        split (the gate/up projection, the lm_head): tread_rows_gemm, weights streamed on the
+        tensor cores; everything else: cuBLAS."""
+        if kernels.rows_gemm_fits(x, w) and kernels.rows_gemm_streams_alone(w):
+            return kernels.rows_gemm(x, w, bias=bias, out=out, accumulate=accumulate)
+        if accumulate:
+            if bias is not None:
+                raise ValueError("linear: accumulate takes no bias")
+            return out.addmm_(x, w.t())
+        y = x @ w.t() if bias is None else torch.addmm(bias, x, w.t())
+        if out is not None:
+            out.copy_(y)
+            return out
+        return y
+
     # -- one layer over rows ----------------------------------------------------------------------
     def qkv(self, l, h):
         p = self.layers[l]
-        return torch.addmm(p["bqkv"], self.rmsnorm(h, p["ln1"], p["ln1_eps"]), p["wqkv"].t())
+        return self.linear(self.rmsnorm(h, p["ln1"], p["ln1_eps"]), p["wqkv"], bias=p["bqkv"])
 
     def kv(self, l, h):
         """Only the k and v columns of layer l's projection, [R, 2 * Hkv * D]: the deviation
@@ -88,7 +111,7 @@ class Qwen2Rows:
         skips the Hq * D query columns."""
         p = self.layers[l]
         nq = self.Hq * self.D
-        return torch.addmm(p["bqkv"][nq:], self.rmsnorm(h, p["ln1"], p["ln1_eps"]), p["wqkv"][nq:].t())
+        return self.linear(self.rmsnorm(h, p["ln1"], p["ln1_eps"]), p["wqkv"][nq:], bias=p["bqkv"][nq:])
 
     def layer(self, l, h, pos, K, V, qkv=None):
         """h: [R, hidden] rows at positions pos (int64 [R]); K, V: layer-l caches [1, Hkv, T, D]
@@ -114,10 +137,10 @@ class Qwen2Rows:
     def layer_tail(self, l, h, o):
         """h + o_proj(o), then h + down(silu(gate) * up) of its RMSNorm (residuals in place)."""
         p = self.layers[l]
-        h.addmm_(o, p["wo"].t())
+        self.linear(o, p["wo"], out=h, accumulate=True)
         x = self.rmsnorm(h, p["ln2"], p["ln2_eps"])
-        a = kernels.silu_mul(x @ p["wgu"].t())
-        return h.addmm_(a, p["wd"].t())
+        a = kernels.silu_mul(self.linear(x, p["wgu"]))
+        return self.linear(a, p["wd"], out=h, accumulate=True)
 
     def run(self, h, pos, Ks, Vs, l0=0, l1=None):
         """Rows h through layers [l0, l1); returns the final hidden rows (h itself is not modified)."""
@@ -129,7 +152,7 @@ class Qwen2Rows:
     def logits(self, h_last):
         """Final RMSNorm + lm_head of the given rows (HF Qwen2Model.norm, Qwen2ForCausalLM.lm_head)."""
         x = self.rmsnorm(h_last, self.norm_w, self.norm_eps)
-        return x @ self.lm_head.t()
+        return self.linear(x, self.lm_head)
 
     def deviation_select(self, k1, v1, K1, V1, cand_pos, budget):
         """Layer-1 deviation of the candidates and the top-`budget` selection (dev, sel_idx, S);

@@ -146,6 +146,8 @@ class TPQwen2Rows(Qwen2Rows):
         self.embed, self.norm_w, self.norm_eps, self.lm_head = embed, norm_w, norm_eps, lm_head
         self.layers = [shard_layer(w, self.Hq_total, self.Hkv_total, self.D, self.rank, self.world) for w in layers]
         self.err = torch.zeros(4, dtype=torch.int32, device=self.device)
+        if self.device.type == "cuda":
+            kernels.rows_gemm_workspace(self.device)  # before any graph capture holds its address
 
     @classmethod
     def from_model(cls, model, group=None):
@@ -193,7 +195,7 @@ class TPQwen2Rows(Qwen2Rows):
 
     def _row_parallel(self, a, w, h, name):
         """h + sum over ranks of a_r @ w_r^T (rank 0 folds the residual into its product)."""
-        out = torch.addmm(h, a, w.t()) if self.rank == 0 else a @ w.t()
+        out = self.linear(a, w, out=h.clone(), accumulate=True) if self.rank == 0 else self.linear(a, w)
         if self.world > 1:
             self._timed(name, lambda: dist.all_reduce(out, group=self.group))
         return out
@@ -204,7 +206,7 @@ class TPQwen2Rows(Qwen2Rows):
         p = self.layers[l]
         h = self._row_parallel(o, p["wo"], h, "o_proj_allreduce")
         x = self.rmsnorm(h, p["ln2"], p["ln2_eps"])
-        a = kernels.silu_mul(x @ p["wgu"].t())
+        a = kernels.silu_mul(self.linear(x, p["wgu"]))
         return self._row_parallel(a, p["wd"], h, "down_proj_allreduce")
 
     def deviation_select(self, k1, v1, K1, V1, cand_pos, budget):
