@@ -97,15 +97,28 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (warp == 0) {
     // ------------------------------------------------------------------ TMA loader (one lane)
     if (lane == 0) {
-      for (int c = c0, i = 0; c < c1; ++c, ++i) {
-        const int s = i % nstages;
-        if (i >= nstages && !wait(&empty[s], (uint32_t)(((i / nstages) - 1) & 1))) break;
+      auto load_w = [&](int i) {
+        const int s = i % nstages, c = c0 + i;
         unsigned char* st = smem + (size_t)s * sbytes;
         mbar_expect_tx(&full[s], (uint32_t)sbytes);
 #pragma unroll
         for (int t = 0; t < kTiles; ++t)
           tma_load_2d(st + t * kWBytes, &tm_w, &full[s], c * kChunk, (pair * kTiles + t) * kFeat);
-        tma_load_2d(st + kTiles * kWBytes, &tm_x, &full[s], c * kChunk, 0);
+      };
+      auto load_x = [&](int i) {
+        tma_load_2d(smem + (size_t)(i % nstages) * sbytes + kTiles * kWBytes, &tm_x, &full[i % nstages],
+                    (c0 + i) * kChunk, 0);
+      };
+      // the weights do not depend on the kernels before this one (launched as a programmatic
+      // dependent): the first ring of them loads while those kernels finish, x only after
+      const int nc = c1 - c0, pre = min(nstages, nc);
+      for (int i = 0; i < pre; ++i) load_w(i);
+      griddep_wait();
+      for (int i = 0; i < pre; ++i) load_x(i);
+      for (int i = pre; i < nc; ++i) {
+        if (!wait(&empty[i % nstages], (uint32_t)(((i / nstages) - 1) & 1))) break;
+        load_w(i);
+        load_x(i);
       }
     }
   } else if (warp == 1) {
@@ -140,6 +153,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     bool ok = __all_sync(0xffffffffu, wait(done, 0));
     if (ok) {
       tc_fence_after();
+      griddep_wait();  // out (read when accumulating, then written) belongs to the kernels before
+      if (tid == 64) griddep_launch_dependents();  // the split-adding launch may start
       float* my_slot = nsplit > 1 ? slots + (size_t)blockIdx.x * slot_floats : nullptr;
 #pragma unroll
       for (int t = 0; t < kTiles; ++t) {
@@ -198,6 +213,7 @@ __global__ void __launch_bounds__(256)
     rows_gemm_finalize_kernel(const float* __restrict__ slots, int M, int N, int npairs, int nsplit,
                               const T* __restrict__ bias, T* out, long long ld_out, int accumulate) {
   constexpr int kPairF = kTiles * kFeat;
+  griddep_wait();  // the splits' slots come from the GEMM launch before
   const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;  // (row, pair, group of 4)
   const long long per_row = (long long)npairs * (kPairF / 4);
   if (i >= per_row * M) return;
@@ -284,15 +300,29 @@ int launch(const void* x, long long ldx, const void* w, long long ldw, const voi
     nsplit = std::max(1, nsplit);
   }
   float* slots = nsplit > 1 ? static_cast<float*>(ws) : nullptr;
-  rows_gemm_kernel<T><<<npairs * nsplit, kThreads, smem_bytes(Mp), st>>>(
-      mw, mx, M, Mp, N, nchunks, nsplit, stages_for(Mp), static_cast<const T*>(bias), static_cast<T*>(out), ld_out,
-      accumulate, slots, err);
-  TREAD_CHECK_LAUNCH("rows_gemm_kernel");
+  // both launches are programmatic dependents of the work before them on the stream: they may
+  // start while it finishes, and wait (griddepcontrol.wait) before touching what it wrote
+  cudaLaunchAttribute pdl[1];
+  pdl[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  pdl[0].val.programmaticStreamSerializationAllowed = 1;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)(npairs * nsplit));
+  cfg.blockDim = dim3(kThreads);
+  cfg.dynamicSmemBytes = smem_bytes(Mp);
+  cfg.stream = st;
+  cfg.attrs = pdl;
+  cfg.numAttrs = 1;
+  TREAD_CHECK_CUDA(cudaLaunchKernelEx(&cfg, rows_gemm_kernel<T>, mw, mx, M, Mp, N, nchunks, nsplit, stages_for(Mp),
+                                     static_cast<const T*>(bias), static_cast<T*>(out), (long long)ld_out, accumulate,
+                                     slots, err));
   if (nsplit > 1) {
     const long long threads = (long long)M * npairs * (kTiles * kFeat / 4);
-    rows_gemm_finalize_kernel<T><<<(unsigned)((threads + 255) / 256), 256, 0, st>>>(
-        slots, M, N, npairs, nsplit, static_cast<const T*>(bias), static_cast<T*>(out), ld_out, accumulate);
-    TREAD_CHECK_LAUNCH("rows_gemm_finalize_kernel");
+    cfg.gridDim = dim3((unsigned)((threads + 255) / 256));
+    cfg.blockDim = dim3(256);
+    cfg.dynamicSmemBytes = 0;
+    TREAD_CHECK_CUDA(cudaLaunchKernelEx(&cfg, rows_gemm_finalize_kernel<T>, static_cast<const float*>(slots), M, N,
+                                       npairs, nsplit, static_cast<const T*>(bias), static_cast<T*>(out),
+                                       (long long)ld_out, accumulate));
   }
   return TREAD_OK;
 }
