@@ -140,16 +140,15 @@ int tread_select_head_norms(const float* norms, int n, int Hkv, int budget, cons
  * library holds until exit; the caller passes the same inputs and the sel_idx / sel_pos outputs
  * as for tread_deviation_topk (the deviation values themselves are not returned).
  *   - n > TREAD_NOALLOC_MAX_CANDIDATES is rejected with TREAD_ERR_INVALID;
- *   - the first call on a device looks up the array's device address (cudaGetSymbolAddress with
- *     that device current), so make that first call before any stream capture;
+ *   - every call looks up the array's device address in the current context
+ *     (cudaGetSymbolAddress), so it stays right after cudaDeviceReset; make the first call on a
+ *     device before any stream capture (it loads the module);
  *   - every call clears the ticket words on `stream` and then reuses the shared array, so calls
  *     that overlap on the GPU (different streams, or different host threads) race: order them;
  *   - err_flag (optional, device unsigned[1], may be NULL) receives this call's out-of-range
  *     flag in stream order: 1 if a candidate position lay outside [0, T_cache) (that candidate's
  *     deviation is NaN and it ranks first), else 0. It is copied out of the shared array, so it
  *     needs no scratch from the caller;
- *   - the array's device address is cached per device for the primary context, so it does not
- *     survive cudaDeviceReset;
  *   - it calls no cudaMalloc / cudaFree.
  */
 #define TREAD_NOALLOC_MAX_CANDIDATES 65536

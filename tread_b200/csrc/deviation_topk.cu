@@ -660,7 +660,6 @@ extern "C" int tread_select_head_norms(const float* norms, int n, int Hkv, int b
 // fp32 deviation of every candidate — lives in one file-scope device array instead, so the call
 // allocates nothing; the caller still passes every input and output.
 
-#include <mutex>
 
 namespace tread {
 namespace {
@@ -672,28 +671,17 @@ constexpr size_t kNoAllocTicketBytes = 256;
 static __device__ __align__(256) unsigned char
     g_selector_scratch[kNoAllocTicketBytes + sizeof(float) * kNoAllocMaxCandidates];
 
-constexpr int kMaxDevices = 128;
-std::mutex g_scratch_mu;
-void* g_scratch_addr[kMaxDevices] = {};  // device address of g_selector_scratch, per device
-
-// Device address of the static scratch on the current device, looked up once per device. The
-// cached address belongs to the device's primary context: it does not survive cudaDeviceReset.
+// Device address of the static scratch in the current context, looked up on every call (a host
+// table lookup once the module is loaded), so that it stays right after the context is torn down
+// and created again (cudaDeviceReset) and the module loads at another address.
 int scratch_address(void** out) {
-  int dev = -1;
-  TREAD_CHECK_CUDA(cudaGetDevice(&dev));
-  TREAD_CHECK_ARG(dev >= 0 && dev < kMaxDevices, "deviation_topk_noalloc: device %d out of range", dev);
-  std::lock_guard<std::mutex> lock(g_scratch_mu);
-  if (g_scratch_addr[dev] == nullptr) {
-    void* p = nullptr;
-    const cudaError_t e = cudaGetSymbolAddress(&p, g_selector_scratch);
-    if (e != cudaSuccess || p == nullptr) {
-      set_error("deviation_topk_noalloc: cudaGetSymbolAddress failed on device %d: %s", dev,
-                cudaGetErrorString(e));
-      return TREAD_ERR_CUDA;
-    }
-    g_scratch_addr[dev] = p;
+  void* p = nullptr;
+  const cudaError_t e = cudaGetSymbolAddress(&p, g_selector_scratch);
+  if (e != cudaSuccess || p == nullptr) {
+    set_error("deviation_topk_noalloc: cudaGetSymbolAddress failed: %s", cudaGetErrorString(e));
+    return TREAD_ERR_CUDA;
   }
-  *out = g_scratch_addr[dev];
+  *out = p;
   return TREAD_OK;
 }
 
