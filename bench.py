@@ -739,9 +739,11 @@ def run_serving_dp(args, dev, world, rank):
     as soon as the previous one's first token is back. A replica serves its queue one request at
     a time (the reference server serialises GPU work, tread/server.py:186-192) and the replicas
     step in lockstep rounds (the rounds are the block-exchange steps), one request each per round.
-    Untimed warm-up rounds fill the stores, then --dp-rounds rounds are timed. A request's TTFT is
-    its queueing time plus its service time (host ids in, first token out, wall clock); the
-    service time alone is reported too. requests/s = N x rounds / the max over ranks of the timed
+    Untimed warm-up rounds fill the stores (10 rounds) and run the clients' queue through one full
+    cycle (64 / N rounds), then --dp-rounds rounds are timed. A request's TTFT is its queueing
+    time plus its service time (host ids in, first token out, wall clock): the time since the same
+    client's previous first token, in the steady state of the closed loop. The service time alone
+    is reported too. requests/s = N x rounds / the max over ranks of the timed
     region's length. Tier transfers are timed with CUDA events on the store's transfer stream
     (spill / fetch GB/s); the fetch overlap is the share of fetch time the compute stream did not
     wait for (it ran under the request's other work: lookups, cold prefills, resident blocks'
@@ -775,9 +777,11 @@ def run_serving_dp(args, dev, world, rank):
 
     from tread_b200.engine import fetch_overlap
 
-    warm = 10
     clients = max(1, 64 // world)  # closed-loop clients this replica serves
-    service, done, st_all = [], [], []
+    # 10 rounds fill the stores, then one full cycle of the clients: every timed request then
+    # waits behind requests of the steady state, not behind the queue as it stood at the start
+    warm = 10 + clients
+    service, done, done_all, st_all = [], [], [], []
     s0 = None
     for rnd in range(warm + args.dp_rounds):
         if rnd == warm:
@@ -794,6 +798,7 @@ def run_serving_dp(args, dev, world, rank):
         int(logits.argmax().item())
         t1 = time.perf_counter()
         del cache
+        done_all.append(t1)
         if rnd >= warm:
             service.append(t1 - t0)
             done.append(t1)
@@ -804,8 +809,9 @@ def run_serving_dp(args, dev, world, rank):
     rates = eng.store.transfer_rates()
     eng.store.timing = False
     eng.fetch_waits = []
-    # FIFO over this replica's clients: request j was sent when request j - clients finished
-    ttft = [done[j] - (done[j - clients] if j >= clients else t_start) for j in range(len(done))]
+    # closed loop, FIFO over this replica's clients: a request was sent when the same client's
+    # previous request (`clients` rounds earlier, warm-up rounds included) had its first token
+    ttft = [done_all[warm + j] - done_all[warm + j - clients] for j in range(len(done))]
     s1 = vars(eng.store.stats)
     d = {k: s1[k] - s0[k] for k in ("hits", "misses", "evictions", "cpu_hits", "offloads")}
     t = torch.tensor(ttft, dtype=torch.float64, device=dev)
