@@ -727,6 +727,15 @@ def run_ttft_tp(args, dev, world, rank, arch, prefix_len, ndocs, doc_len, q_len)
     return out
 
 
+def closed_loop_ttft(done_all, warm, clients):
+    """TTFT of each timed request of one replica: its first-token time minus the first-token time
+    of the same client's previous request. Clients are served FIFO, one request per round, so that
+    request ran `clients` rounds earlier (warm-up rounds included; warm >= clients)."""
+    if warm < clients:
+        raise ValueError("the warm-up must cover one full cycle of the clients")
+    return [done_all[j] - done_all[j - clients] for j in range(warm, len(done_all))]
+
+
 def run_serving_dp(args, dev, world, rank):
     """N data-parallel replicas of a random-init Qwen2.5-7B architecture
     (bf16), doc blocks sharded by content hash (tread_b200.dp.ShardedEngine). Pool of 512 docs,
@@ -809,9 +818,7 @@ def run_serving_dp(args, dev, world, rank):
     rates = eng.store.transfer_rates()
     eng.store.timing = False
     eng.fetch_waits = []
-    # closed loop, FIFO over this replica's clients: a request was sent when the same client's
-    # previous request (`clients` rounds earlier, warm-up rounds included) had its first token
-    ttft = [done_all[warm + j] - done_all[warm + j - clients] for j in range(len(done))]
+    ttft = closed_loop_ttft(done_all, warm, clients)
     s1 = vars(eng.store.stats)
     d = {k: s1[k] - s0[k] for k in ("hits", "misses", "evictions", "cpu_hits", "offloads")}
     t = torch.tensor(ttft, dtype=torch.float64, device=dev)

@@ -6,6 +6,8 @@ import os
 import subprocess
 import sys
 
+import pytest
+
 ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
 
 
@@ -31,3 +33,17 @@ def test_reference_arm_line():
 
 def test_reference_arm_other_ranks_silent():
     assert _run({"RANK": "1"}) == []
+
+
+def test_serving_ttft_is_measured_in_the_closed_loop_steady_state():
+    """A timed request's TTFT runs from the same client's previous first token, `clients` rounds
+    earlier, warm-up rounds included; a warm-up shorter than one client cycle is refused."""
+    sys.path.insert(0, ROOT)
+    import bench
+
+    done = [float(t) for t in range(10)]  # one request per round, first token at t = round
+    assert bench.closed_loop_ttft(done, warm=4, clients=3) == [3.0] * 6
+    done = done[:7] + [8.5, 9.5, 10.5]  # round 7 takes 2.5: the requests finishing after it wait longer
+    assert bench.closed_loop_ttft(done, warm=4, clients=3) == [3.0, 3.0, 3.0, 4.5, 4.5, 4.5]
+    with pytest.raises(ValueError):
+        bench.closed_loop_ttft(done, warm=2, clients=3)
