@@ -65,6 +65,7 @@ def parse():
     ap.add_argument("--only", choices=["attention", "selector", "ttft", "rows_gemm"], default=None,
                     help="run one kernel microbench alone (for profiler captures) and print its timing")
     ap.add_argument("--ttft-reps", type=int, default=5, help="timed warm requests per recompute ratio")
+    ap.add_argument("--ttft-ratio", type=float, default=0.2, help="recompute ratio of --only ttft's request")
     ap.add_argument("--no-dp", action="store_true", help="skip the configs[4] hash-sharded replica serving leg")
     ap.add_argument("--dp-rounds", type=int, default=30, help="timed serving rounds (one request per replica each)")
     ap.add_argument("--no-tp", action="store_true",
@@ -1058,7 +1059,8 @@ def run_e2e(args, dev, pool_k, pool_v, ids, deltas, inv, world, rank):
 
 
 def run_only_ttft(args):
-    """One configs[2] request at 20% recompute (eager), after a cold pass and --warmup warm requests,
+    """One configs[2] request at --ttft-ratio recompute (eager; 0.2 by default), after a cold pass
+    and --warmup warm requests,
     bracketed by cudaProfilerStart/Stop so that a profiler started with --profile-from-start off
     sees exactly that request's launches."""
     from tread_b200 import BlockStore, Engine
@@ -1075,12 +1077,12 @@ def run_only_ttft(args):
     eng.prefill(prefix, docs, query)
     pg = torch.Generator().manual_seed(args.seed + 5)
     for _ in range(max(1, args.warmup)):
-        eng.prefill(prefix, [docs[i] for i in torch.randperm(16, generator=pg).tolist()], query, ratio=0.2)
+        eng.prefill(prefix, [docs[i] for i in torch.randperm(16, generator=pg).tolist()], query, ratio=args.ttft_ratio)
     order = [docs[i] for i in torch.randperm(16, generator=pg).tolist()]
     torch.cuda.synchronize(dev)
     torch.cuda.cudart().cudaProfilerStart()
     t0 = time.perf_counter()
-    logits, _, st = eng.prefill(prefix, order, query, ratio=0.2)
+    logits, _, st = eng.prefill(prefix, order, query, ratio=args.ttft_ratio)
     int(logits.argmax().item())
     t1 = time.perf_counter()
     torch.cuda.cudart().cudaProfilerStop()
