@@ -83,13 +83,14 @@ class Qwen2Rows:
         return F.embedding(ids, self.embed)
 
     @staticmethod
-    def linear(x, w, bias=None, out=None, accumulate=False):
+    def linear(x, w, bias=None, out=None, accumulate=False, err=None):
         """x @ w^T (+ bias), or out + x @ w^T in place when `accumulate`, rounded once (HF Linear /
         torch.addmm). Up to 128 rows against a weight wide enough to fill every SM without a K
         split (the gate/up projection, the lm_head): tread_rows_gemm, weights streamed on the
-        tensor cores; everything else: cuBLAS."""
+        tensor cores; everything else: cuBLAS. `err`: the device error word in which a bounded
+        wait of the tensor-core kernel that gave up sets bit 2."""
         if kernels.rows_gemm_fits(x, w) and kernels.rows_gemm_streams_alone(w):
-            return kernels.rows_gemm(x, w, bias=bias, out=out, accumulate=accumulate)
+            return kernels.rows_gemm(x, w, bias=bias, out=out, accumulate=accumulate, err=err)
         if accumulate:
             if bias is not None:
                 raise ValueError("linear: accumulate takes no bias")
@@ -103,7 +104,7 @@ class Qwen2Rows:
     # -- one layer over rows ----------------------------------------------------------------------
     def qkv(self, l, h):
         p = self.layers[l]
-        return self.linear(self.rmsnorm(h, p["ln1"], p["ln1_eps"]), p["wqkv"], bias=p["bqkv"])
+        return self.linear(self.rmsnorm(h, p["ln1"], p["ln1_eps"]), p["wqkv"], bias=p["bqkv"], err=self.err)
 
     def kv(self, l, h):
         """Only the k and v columns of layer l's projection, [R, 2 * Hkv * D]: the deviation
@@ -111,7 +112,8 @@ class Qwen2Rows:
         skips the Hq * D query columns."""
         p = self.layers[l]
         nq = self.Hq * self.D
-        return self.linear(self.rmsnorm(h, p["ln1"], p["ln1_eps"]), p["wqkv"][nq:], bias=p["bqkv"][nq:])
+        return self.linear(self.rmsnorm(h, p["ln1"], p["ln1_eps"]), p["wqkv"][nq:], bias=p["bqkv"][nq:],
+                           err=self.err)
 
     def layer(self, l, h, pos, K, V, qkv=None):
         """h: [R, hidden] rows at positions pos (int64 [R]); K, V: layer-l caches [1, Hkv, T, D]
@@ -137,10 +139,10 @@ class Qwen2Rows:
     def layer_tail(self, l, h, o):
         """h + o_proj(o), then h + down(silu(gate) * up) of its RMSNorm (residuals in place)."""
         p = self.layers[l]
-        self.linear(o, p["wo"], out=h, accumulate=True)
+        self.linear(o, p["wo"], out=h, accumulate=True, err=self.err)
         x = self.rmsnorm(h, p["ln2"], p["ln2_eps"])
-        a = kernels.silu_mul(self.linear(x, p["wgu"]))
-        return self.linear(a, p["wd"], out=h, accumulate=True)
+        a = kernels.silu_mul(self.linear(x, p["wgu"], err=self.err))
+        return self.linear(a, p["wd"], out=h, accumulate=True, err=self.err)
 
     def run(self, h, pos, Ks, Vs, l0=0, l1=None):
         """Rows h through layers [l0, l1); returns the final hidden rows (h itself is not modified)."""
@@ -152,7 +154,7 @@ class Qwen2Rows:
     def logits(self, h_last):
         """Final RMSNorm + lm_head of the given rows (HF Qwen2Model.norm, Qwen2ForCausalLM.lm_head)."""
         x = self.rmsnorm(h_last, self.norm_w, self.norm_eps)
-        return self.linear(x, self.lm_head)
+        return self.linear(x, self.lm_head, err=self.err)
 
     def deviation_select(self, k1, v1, K1, V1, cand_pos, budget):
         """Layer-1 deviation of the candidates and the top-`budget` selection (dev, sel_idx, S);

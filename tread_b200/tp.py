@@ -195,7 +195,8 @@ class TPQwen2Rows(Qwen2Rows):
 
     def _row_parallel(self, a, w, h, name):
         """h + sum over ranks of a_r @ w_r^T (rank 0 folds the residual into its product)."""
-        out = self.linear(a, w, out=h.clone(), accumulate=True) if self.rank == 0 else self.linear(a, w)
+        out = (self.linear(a, w, out=h.clone(), accumulate=True, err=self.err) if self.rank == 0
+               else self.linear(a, w, err=self.err))
         if self.world > 1:
             self._timed(name, lambda: dist.all_reduce(out, group=self.group))
         return out
@@ -206,7 +207,7 @@ class TPQwen2Rows(Qwen2Rows):
         p = self.layers[l]
         h = self._row_parallel(o, p["wo"], h, "o_proj_allreduce")
         x = self.rmsnorm(h, p["ln2"], p["ln2_eps"])
-        a = kernels.silu_mul(self.linear(x, p["wgu"]))
+        a = kernels.silu_mul(self.linear(x, p["wgu"], err=self.err))
         return self._row_parallel(a, p["wd"], h, "down_proj_allreduce")
 
     def deviation_select(self, k1, v1, K1, V1, cand_pos, budget):
