@@ -61,6 +61,7 @@ def parse():
     ap.add_argument("--seed", type=int, default=0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=10.0, help="CPU baseline sample budget")
+    ap.add_argument("--cpu-pool", type=int, default=16, help="host blocks the CPU path draws from")
     ap.add_argument("--no-ttft", action="store_true", help="skip the configs[2] 7B TTFT leg")
     ap.add_argument("--only", choices=["attention", "selector", "ttft", "rows_gemm"], default=None,
                     help="run one kernel microbench alone (for profiler captures) and print its timing")
@@ -405,7 +406,7 @@ def run_reference(args):
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return 0
-    r = cpu_assembly_rate(args.warmup + args.steps, 0.0, args.seed, args.blocks)
+    r = cpu_assembly_rate(args.warmup + args.steps, 0.0, args.seed, args.blocks, args.cpu_pool)
     line = {
         "impl": "reference", "metric": METRIC, "value": round(r["gbs"], 3), "unit": "GB/s", "n_gpus": args.gpus,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(r["ms"], 3), "higher_is_better": True,
@@ -512,7 +513,7 @@ def run_gpu(args):
             ttft["cpu_baseline"] = run_ttft_cpu(args)
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        r = cpu_assembly_rate(3, args.cpu_seconds, args.seed, args.blocks)
+        r = cpu_assembly_rate(3, args.cpu_seconds, args.seed, args.blocks, args.cpu_pool)
         cpu = {"value": round(r["gbs"], 3), "unit": "GB/s", "cores": r["cores"], "kind": "port",
                "sample": f"median of {r['steps']} full steps (~{args.cpu_seconds:.0f} s) of the same workload, "
                          f"{args.blocks} blocks from a {r['host_pool']}-block host pool, oracle C restatement"}

@@ -13,8 +13,10 @@ ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
 
 def _run(env_extra):
     env = dict(os.environ, **env_extra)
+    # a small sample (4 blocks from a 4-block host pool): these tests check the line's contract
     out = subprocess.run([sys.executable, os.path.join(ROOT, "bench.py"), "--impl", "reference", "--steps", "2",
-                          "--warmup", "1"], capture_output=True, text=True, env=env, timeout=600, cwd=ROOT)
+                          "--warmup", "1", "--blocks", "4", "--cpu-pool", "4"], capture_output=True, text=True,
+                         env=env, timeout=600, cwd=ROOT)
     assert out.returncode == 0, out.stderr[-2000:]
     return [l for l in out.stdout.splitlines() if l.startswith("{")]
 
