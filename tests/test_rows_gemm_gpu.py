@@ -83,3 +83,41 @@ def test_rows_gemm_strided_views():
     got = kernels.rows_gemm(x, wk, bias=b[3584:], out=out[:, 512:1536])
     _check(got, x.float() @ wk.float().t() + b[3584:].float(), torch.bfloat16)
     assert int(out[:, :512].count_nonzero()) == 0 and int(out[:, 1536:].count_nonzero()) == 0
+
+
+def test_query_forward_streams_the_wide_weights_through_rows_gemm(monkeypatch):
+    """With the query rows alone (ratio 0), the engine's layer pass sends the gate/up projection
+    and the lm_head of the 7B architecture to tread_rows_gemm, and the rest to cuBLAS; the logits
+    match the same request with every projection on cuBLAS."""
+    import torch.nn.functional as F
+
+    from tread_b200 import BlockStore, Engine
+    from tread_b200.configs import random_model, random_tokens
+
+    if torch.cuda.get_device_properties(0).multi_processor_count * 256 > 37888:
+        pytest.skip("the 7B gate/up weight fills every SM without a K split only up to 148 SMs")
+    model = random_model("qwen2.5-7b", dtype=torch.bfloat16, device=DEV, layers=2, init_on_device=True)
+    V = model.config.vocab_size
+    g = torch.Generator().manual_seed(7)
+    prefix, query = random_tokens(64, V, g), random_tokens(16, V, g)
+    docs = [random_tokens(200, V, g) for _ in range(3)]
+    eng = Engine(model, BlockStore(8 << 30))
+    eng.prefill(prefix, docs, query)  # cold: fills the store
+    calls = []
+    orig = kernels.rows_gemm
+
+    def spy(x, w, *a, **kw):
+        calls.append(tuple(w.shape))
+        return orig(x, w, *a, **kw)
+
+    monkeypatch.setattr(kernels, "rows_gemm", spy)
+    logits, _, st = eng.prefill(prefix, docs[::-1], query)
+    assert st.hits == 4 and st.misses == 0
+    assert sorted(calls) == sorted([(2 * 18944, 3584)] * 2 + [(V, 3584)])  # gate/up of both layers, lm_head
+    monkeypatch.setattr(kernels, "rows_gemm_streams_alone", lambda w: False)  # every projection on cuBLAS
+    calls.clear()
+    ref, _, _ = eng.prefill(prefix, docs[::-1], query)
+    assert calls == []
+    kl = F.kl_div(F.log_softmax(ref.float(), -1), F.log_softmax(logits.float(), -1), log_target=True,
+                  reduction="sum")
+    assert float(kl) < 1e-3
