@@ -121,3 +121,15 @@ def test_query_forward_streams_the_wide_weights_through_rows_gemm(monkeypatch):
     kl = F.kl_div(F.log_softmax(ref.float(), -1), F.log_softmax(logits.float(), -1), log_target=True,
                   reduction="sum")
     assert float(kl) < 1e-3
+
+
+def test_rows_gemm_refuses_operands_off_the_device():
+    """A weight, bias or output that is not on x's device is refused before anything launches."""
+    x, w, b, o = _case(4, 256, 64, torch.bfloat16, 5)
+    with pytest.raises(ValueError):
+        kernels.rows_gemm(x, w.cpu())
+    with pytest.raises(ValueError):
+        kernels.rows_gemm(x, w, bias=b.cpu())
+    with pytest.raises(ValueError):
+        kernels.rows_gemm(x, w, out=o.cpu())
+    assert not kernels.rows_gemm_fits(x, w.cpu())

@@ -405,10 +405,10 @@ def rows_gemm_workspace(device):
 
 
 def rows_gemm_fits(x, w):
-    """True when x [M, K] @ w[N, K]^T can run on tread_rows_gemm: 1..128 rows, bf16 / fp16, unit
-    column strides, 16-byte aligned rows and K a multiple of 8."""
+    """True when x [M, K] @ w[N, K]^T can run on tread_rows_gemm: both on one CUDA device, 1..128
+    rows, bf16 / fp16, unit column strides, 16-byte aligned rows and K a multiple of 8."""
     return (x.dim() == 2 and w.dim() == 2 and 0 < x.shape[0] <= ROWS_GEMM_MAX_ROWS and x.is_cuda
-            and x.dtype in (torch.bfloat16, torch.float16) and w.dtype == x.dtype and x.shape[1] == w.shape[1]
+            and w.device == x.device and x.dtype in (torch.bfloat16, torch.float16) and w.dtype == x.dtype and x.shape[1] == w.shape[1]
             and x.stride(1) == 1 and w.stride(1) == 1 and x.shape[1] % 8 == 0 and x.stride(0) % 8 == 0
             and w.stride(0) % 8 == 0 and x.data_ptr() % 16 == 0 and w.data_ptr() % 16 == 0)
 
@@ -419,8 +419,8 @@ _sm_counts = {}
 def rows_gemm_streams_alone(w):
     """True when w [N, K] has at least one pair of 128-feature tiles per SM, so tread_rows_gemm
     streams it in one wave without a K split. Measured on B200 (CUDA-graph replay, 7B shapes),
-    those weights (gate/up: 37888 x 3584; lm_head: 151936 x 3584) run at 0.88-0.97 of the HBM copy
-    peak, 1-2 % ahead of cuBLAS. The narrower ones need a K split and a second launch, and lose
+    those weights (gate/up: 37888 x 3584; lm_head: 151936 x 3584) run at 0.90-1.00 of the HBM copy
+    peak, 2-5 % ahead of cuBLAS. The narrower ones need a K split and a second launch, and lose
     about 4 us to cuBLAS on a 26-33 MB weight."""
     idx = w.device.index
     n = _sm_counts.get(idx)
@@ -442,14 +442,15 @@ def rows_gemm(x, w, bias=None, out=None, accumulate=False, err=None, stream=None
                          "16-byte aligned rows and K % 8 == 0")
     M, K = x.shape
     N = w.shape[0]
-    if bias is not None and (bias.shape != (N,) or bias.dtype != x.dtype or not bias.is_contiguous()):
-        raise ValueError("rows_gemm: bias must be a contiguous [N] tensor of x's dtype")
+    if bias is not None and (bias.shape != (N,) or bias.dtype != x.dtype or not bias.is_contiguous()
+                             or bias.device != x.device):
+        raise ValueError("rows_gemm: bias must be a contiguous [N] tensor of x's dtype on x's device")
     if out is None:
         if accumulate:
             raise ValueError("rows_gemm: accumulate needs out")
         out = torch.empty(M, N, dtype=x.dtype, device=x.device)
-    elif out.shape != (M, N) or out.dtype != x.dtype or out.stride(1) != 1:
-        raise ValueError("rows_gemm: out must be [M, N] of x's dtype with unit column stride")
+    elif out.shape != (M, N) or out.dtype != x.dtype or out.stride(1) != 1 or out.device != x.device:
+        raise ValueError("rows_gemm: out must be [M, N] of x's dtype with unit column stride, on x's device")
     ws = rows_gemm_workspace(x.device) if split else None
     with torch.cuda.device(x.device):
         rc = C.lib().tread_rows_gemm(x.data_ptr(), x.stride(0), w.data_ptr(), w.stride(0),
