@@ -131,3 +131,11 @@ def f32_array(vals):
 def require_cuda(t, name):
     if not t.is_cuda:
         raise ValueError(f"{name} must be a CUDA tensor (got {t.device}); tread_b200 has no CPU path")
+
+
+def same_device(ref, **tensors):
+    """Every tensor given (None skips) must sit on ref's device: the kernels dereference them all
+    there, so a host or other-GPU tensor is refused before anything launches."""
+    for name, t in tensors.items():
+        if t is not None and t.device != ref.device:
+            raise ValueError(f"{name} is on {t.device}, the call's other tensors on {ref.device}")

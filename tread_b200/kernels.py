@@ -37,6 +37,7 @@ class RopeAppendPlan:
                 raise ValueError(f"{nm} must be contiguous")
         if out_k.shape != out_v.shape or out_k.dtype != out_v.dtype:
             raise ValueError("out_k and out_v must have the same shape and dtype")
+        C.same_device(out_k, out_v=out_v)
         D = out_k.shape[-1]
         T_out = out_k.shape[-2]
         LH = out_k.numel() // (T_out * D) if T_out * D else 0
@@ -48,6 +49,7 @@ class RopeAppendPlan:
                 raise ValueError(f"segment K/V shape {tuple(K.shape)} does not match output {tuple(out_k.shape)}")
             if K.dtype != out_k.dtype or V.dtype != out_k.dtype:
                 raise TypeError("segment dtype differs from the output dtype")
+            C.same_device(out_k, K=K, V=V)
             if K.device != out_k.device or V.device != out_k.device:
                 raise ValueError("segment and output on different devices")
             kp.append(K.data_ptr())
@@ -183,6 +185,7 @@ def deviation_topk(k1, v1, K1, V1, cand_pos, budget, dev_out=None, sel_idx=None,
     V1, c_st2, c_sh2 = _rows_view(V1, "V1")
     if (f_st, f_sh) != (f_st2, f_sh2) or (c_st, c_sh) != (c_st2, c_sh2):
         raise ValueError("k1/v1 (and K1/V1) must share strides")
+    C.same_device(k1, v1=v1, K1=K1, V1=V1, cand_pos=cand_pos, ws=ws)
     H, n, D = k1.shape
     if v1.shape != k1.shape or K1.shape[0] != H or K1.shape[2] != D or V1.shape != K1.shape:
         raise ValueError("shape mismatch between fresh rows and cache")
@@ -200,6 +203,7 @@ def deviation_topk(k1, v1, K1, V1, cand_pos, budget, dev_out=None, sel_idx=None,
         sel_idx = torch.empty(budget, dtype=torch.int64, device=dev)
     if sel_pos is None:
         sel_pos = torch.empty(budget, dtype=torch.int64, device=dev)
+    C.same_device(k1, dev_out=dev_out, sel_idx=sel_idx, sel_pos=sel_pos)
     if ws is None:
         ws = workspace(dev, stream)
     if n == 0:
@@ -223,6 +227,7 @@ def deviation_head_norms(k1, v1, K1, V1, cand_pos, norms_out=None, ws=None, stre
     V1, c_st2, c_sh2 = _rows_view(V1, "V1")
     if (f_st, f_sh) != (f_st2, f_sh2) or (c_st, c_sh) != (c_st2, c_sh2):
         raise ValueError("k1/v1 (and K1/V1) must share strides")
+    C.same_device(k1, v1=v1, K1=K1, V1=V1, cand_pos=cand_pos, ws=ws)
     H, n, D = k1.shape
     if v1.shape != k1.shape or K1.shape[0] != H or K1.shape[2] != D or V1.shape != K1.shape:
         raise ValueError("shape mismatch between fresh rows and cache")
@@ -233,8 +238,9 @@ def deviation_head_norms(k1, v1, K1, V1, cand_pos, norms_out=None, ws=None, stre
     dev = k1.device
     if norms_out is None:
         norms_out = torch.empty(2, H, n, dtype=torch.float32, device=dev)
-    elif norms_out.shape != (2, H, n) or norms_out.dtype != torch.float32 or not norms_out.is_contiguous():
-        raise ValueError("norms_out must be a contiguous fp32 [2, H, n] tensor")
+    elif (norms_out.shape != (2, H, n) or norms_out.dtype != torch.float32 or not norms_out.is_contiguous()
+          or norms_out.device != k1.device):
+        raise ValueError("norms_out must be a contiguous fp32 [2, H, n] tensor on k1's device")
     if ws is None:
         ws = workspace(dev, stream)
     if n == 0:
@@ -253,6 +259,7 @@ def select_head_norms(norms, cand_pos, budget, dev_out=None, sel_idx=None, sel_p
     order (an all-gather of `deviation_head_norms` over the KV-head ranks). Same results as
     `deviation_topk` on a single GPU holding all heads."""
     C.require_cuda(norms, "norms")
+    C.same_device(norms, cand_pos=cand_pos, dev_out=dev_out, sel_idx=sel_idx, sel_pos=sel_pos, ws=ws)
     if norms.dim() != 3 or norms.shape[0] != 2 or norms.dtype != torch.float32 or not norms.is_contiguous():
         raise ValueError("norms must be a contiguous fp32 [2, H, n] tensor")
     _, H, n = norms.shape
@@ -303,6 +310,7 @@ def rope_rows(qkv, pos, Hq, Hkv, D, q_out, K, V, inv_freq, attn_scaling=1.0, err
     C.require_cuda(qkv, "qkv")
     K = _layer_cache(K, "K")
     V = _layer_cache(V, "V")
+    C.same_device(qkv, pos=pos, q_out=q_out, K=K, V=V, err=err)
     R = qkv.shape[0]
     if qkv.dim() != 2 or qkv.stride(1) != 1:
         raise ValueError("qkv must be 2-D with unit column stride")
@@ -362,6 +370,7 @@ def attn_rows(q, K, V, pos, out=None, sm_scale=None, err=None, stream=None, cuda
     C.require_cuda(q, "q")
     K = _layer_cache(K, "K")
     V = _layer_cache(V, "V")
+    C.same_device(q, K=K, V=V, pos=pos, out=out, err=err)
     R, Hq, D = q.shape
     Hkv = K.shape[0]
     if not q.is_contiguous() or K.shape != V.shape or K.stride(0) != V.stride(0) or K.shape[2] != D:
@@ -437,6 +446,7 @@ def rows_gemm(x, w, bias=None, out=None, accumulate=False, err=None, stream=None
     through the device's shared workspace; the splits are added in a fixed order, so results are
     deterministic."""
     C.require_cuda(x, "x")
+    C.same_device(x, w=w, bias=bias, out=out, err=err)
     if not rows_gemm_fits(x, w):
         raise ValueError("rows_gemm: x [M <= 128, K] and w [N, K] must be bf16/fp16 with unit column strides, "
                          "16-byte aligned rows and K % 8 == 0")
@@ -467,6 +477,7 @@ def rows_gemm(x, w, bias=None, out=None, accumulate=False, err=None, stream=None
 def rmsnorm(x, weight, eps, out=None, stream=None):
     """HF Qwen2RMSNorm over the rows of x [R, H] (unit column stride) in one pass."""
     C.require_cuda(x, "x")
+    C.same_device(x, weight=weight, out=out)
     if x.dim() != 2 or x.stride(1) != 1 or weight.shape != (x.shape[1],) or weight.dtype != x.dtype:
         raise ValueError("rmsnorm: x must be [R, H] with unit column stride and weight [H] of x's dtype")
     if out is None:
@@ -482,6 +493,7 @@ def rmsnorm(x, weight, eps, out=None, stream=None):
 def silu_mul(gate_up, out=None, stream=None):
     """silu(g) * u of HF Qwen2MLP, gate_up = [g | u] of shape [R, 2I] (unit column stride)."""
     C.require_cuda(gate_up, "gate_up")
+    C.same_device(gate_up, out=out)
     if gate_up.dim() != 2 or gate_up.stride(1) != 1 or gate_up.shape[1] % 2:
         raise ValueError("silu_mul: gate_up must be [R, 2I] with unit column stride")
     R, I = gate_up.shape[0], gate_up.shape[1] // 2
